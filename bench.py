@@ -1,0 +1,544 @@
+"""Benchmark of the B200 hot path behind the VC runtime API.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--only gemm,fa_causal,fa_bf16,stream,fa_f32]
+
+One JSON line on rank 0. The headline workload is the dense GEMM
+C = A*B, M = N = K = 4096, fp16 inputs drawn U[-1, 1), fp32 accumulate and
+output (weak scaling: every rank runs its own 4096-row block). A step is a
+batch of GEMMS_PER_STEP such products; inputs rotate over 4 buffer sets
+(512 MiB, larger than the 126 MB L2), so every product reads cold operands.
+The other benchmark configurations ride along in "also":
+  fa_causal  flash-attention fwd fp16, B=8, H=16, N=4096, d=128, causal
+  fa_bf16    flash-attention fwd bf16, B=32, H=32, N=8192, d=128, sharded
+             over ranks by batch x heads (strong scaling)
+  stream     vadd c = a + b then sum(c), n = 2^30 fp32, sharded contiguously
+             over ranks, fp64 partials combined by one NCCL all-reduce
+  fa_f32     flash-attention fwd fp32, B=1, H=1, N=256, d=64 (the demo's
+             precision; latency bound)
+Under torchrun (N > 1) ranks time on the device with CUDA events between
+barriers; rank 0 prints the max over ranks.
+
+`--impl reference` times the reference's own CPU algorithm for the headline
+workload (the oracle's restatement of the demos' host loops, all host
+threads) on a bounded sample, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "attn-fwd & GEMM TFLOP/s (% of B200 dense peak), reduce GB/s, at 1/2/4/8 GPU"
+GEMM_N = 4096
+GEMMS_PER_STEP = 100
+ROTATE = 4
+LOG2E = 1.4426950408889634
+
+
+# ---------------------------------------------------------------- helpers
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return {"hbm": p["hbm_gbs"], "bf16": p["bf16_tflops"],
+                "bf16_sustained": p["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def traffic_table():
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        return json.load(open(path))
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi samples (every 100 ms) while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_uuid: str):
+        self.uuid = device_uuid
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[3:7]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, backend="nccl"):
+        import torch
+        import torch.distributed as dist
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group(backend, timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def shard(total: int, world: int, rank: int):
+    """Contiguous [begin, end) share of `total` units for `rank`."""
+    base, rem = divmod(total, world)
+    begin = rank * base + min(rank, rem)
+    return begin, begin + base + (1 if rank < rem else 0)
+
+
+def check(err, what):
+    if int(err) != 0:
+        raise RuntimeError(f"{what} failed with VCError {int(err)}")
+
+
+def timed(dist, stream, fn, steps, warmup, sampler=None):
+    """Run fn() warmup times, then time `steps` calls with CUDA events on
+    `stream` between barriers; returns the max over ranks, in ms."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    return dist.max(e0.elapsed_time(e1))
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+# ---------------------------------------------------------------- workloads
+def gemm_workload(vc, dist, steps, warmup, pk, device_uuid, want_e2e=True):
+    import torch
+    N = GEMM_N
+    g = torch.Generator(device="cuda").manual_seed(1 + dist.rank)
+    sets = []
+    for _ in range(ROTATE):
+        A = (torch.rand(N, N, device="cuda", generator=g) * 2 - 1).half()
+        B = (torch.rand(N, N, device="cuda", generator=g) * 2 - 1).half()
+        C = torch.empty(N, N, device="cuda", dtype=torch.float32)
+        sets.append((A, B, C))
+    stream = torch.cuda.current_stream()
+    state = {"i": 0}
+
+    def one():
+        A, B, C = sets[state["i"] % ROTATE]
+        state["i"] += 1
+        check(vc.gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), None, N, N, N, N, N, N, 0,
+                      vc.Dtype.F16, True, stream.cuda_stream), "vc_gemm")
+
+    def step():
+        for _ in range(GEMMS_PER_STEP):
+            one()
+
+    # Quick parity guard on the first set (row sample vs torch fp32 matmul).
+    one()
+    torch.cuda.synchronize()
+    A, B, C = sets[0]
+    ref = A[:64].float() @ B.float()
+    err = (C[:64] - ref).abs().max().item()
+    if not err <= 1e-3 * math.sqrt(N):
+        raise RuntimeError(f"GEMM parity guard failed: max err {err}")
+
+    sampler = ClockSampler(device_uuid)
+    ms = timed(dist, stream, step, steps, warmup, sampler)
+    flop_step = 2.0 * N ** 3 * GEMMS_PER_STEP
+    per_launch_ms = ms / (steps * GEMMS_PER_STEP)
+    value = flop_step * steps * dist.world / (ms * 1e-3) / 1e12
+    achieved = 2.0 * N ** 3 / (per_launch_ms * 1e-3) / 1e12
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s",
+        "ms_per_step": round(ms / steps, 4),
+        "per_launch_ms": round(per_launch_ms, 5),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16"],
+                     "unit": "TFLOP/s", "frac": round(achieved / pk["bf16"], 4),
+                     "peak_kind": f"bf16 dense burst ({pk['source']})",
+                     "traffic": traffic_table().get("gemm_f16_4096")},
+        "clocks": sampler.summary(),
+        "gpu_launches": steps * GEMMS_PER_STEP,
+    }
+    if want_e2e:
+        out["e2e"] = gemm_e2e(vc, dist, steps=max(3, min(steps, 10)), warmup=2)
+    del sets
+    torch.cuda.empty_cache()
+    return out
+
+
+def gemm_e2e(vc, dist, steps, warmup):
+    """The same GEMM through the reference-facing API: pinned host A, B ->
+    vcMemcpyAsyncS H2D -> vcLaunchKernel('vc.gemm') -> vcMemcpyAsyncS D2H of
+    C, all on one stream, timed with CUDA events around each whole step."""
+    import torch
+    N = GEMM_N
+    nb16, nb32 = N * N * 2, N * N * 4
+    err, hA = vc.vcMallocHost(nb16)
+    check(err, "vcMallocHost")
+    err, hB = vc.vcMallocHost(nb16)
+    err, hC = vc.vcMallocHost(nb32)
+    rng = np.random.default_rng(100 + dist.rank)
+    a = (rng.random(N * N, dtype=np.float32) * 2 - 1).astype(np.float16)
+    b = (rng.random(N * N, dtype=np.float32) * 2 - 1).astype(np.float16)
+    import ctypes
+    ctypes.memmove(hA, a.ctypes.data, nb16)
+    ctypes.memmove(hB, b.ctypes.data, nb16)
+    err, dA = vc.vcMalloc(nb16)
+    err, dB = vc.vcMalloc(nb16)
+    err, dC = vc.vcMalloc(nb32)
+    err, s = vc.vcStreamCreate()
+    err, k = vc.vcGetKernel("vc.gemm")
+    args = [vc.ptr(dA), vc.ptr(dB), vc.ptr(dC), vc.ptr(0), vc.i32(N), vc.i32(N), vc.i32(N),
+            vc.i64(N), vc.i64(N), vc.i64(N), vc.i64(0), vc.i32(int(vc.Dtype.F16)), vc.i32(1)]
+    H2D, D2H = vc.VCMemcpyKind.HostToDevice, vc.VCMemcpyKind.DeviceToHost
+
+    def step():
+        check(vc.vcMemcpyAsyncS(dA, hA, nb16, H2D, s), "H2D A")
+        check(vc.vcMemcpyAsyncS(dB, hB, nb16, H2D, s), "H2D B")
+        check(vc.vcLaunchKernel(k, 1, 1, args, s), "launch vc.gemm")
+        check(vc.vcMemcpyAsyncS(hC, dC, nb32, D2H, s), "D2H C")
+
+    for _ in range(warmup):
+        step()
+    check(vc.vcStreamSynchronize(s), "sync")
+    dist.barrier()
+    err, e0 = vc.vcEventCreate()
+    err, e1 = vc.vcEventCreate()
+    vc.vcEventRecord(e0, s)
+    for _ in range(steps):
+        step()
+    vc.vcEventRecord(e1, s)
+    check(vc.vcEventSynchronize(e1), "event sync")
+    err, ms = vc.vcEventElapsedTime(e0, e1)
+    check(err, "elapsed")
+    ms = dist.max(ms)
+    c_row = np.frombuffer((ctypes.c_float * N).from_address(hC), np.float32)
+    ref = a.reshape(N, N)[0].astype(np.float64) @ b.reshape(N, N).astype(np.float64)
+    if not np.abs(c_row - ref).max() <= 1e-3 * math.sqrt(N):
+        raise RuntimeError("e2e GEMM result check failed")
+    for p in (dA, dB, dC):
+        vc.vcFree(p)
+    for p in (hA, hB, hC):
+        vc.vcFree(p)
+    vc.vcEventDestroy(e0)
+    vc.vcEventDestroy(e1)
+    vc.vcStreamDestroy(s)
+    vc.vcReleaseKernel(k)
+    value = 2.0 * N ** 3 * steps * dist.world / (ms * 1e-3) / 1e12
+    return {"value": round(value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * nb16,
+            "d2h_bytes_per_step": nb32, "ms_per_step": round(ms / steps, 4),
+            "path": "vcMallocHost + vcMemcpyAsyncS + vcLaunchKernel(vc.gemm) + vcMemcpyAsyncS"}
+
+
+def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk, shard_bh):
+    import torch
+    BH = B * H
+    b0, b1 = shard(BH, dist.world, dist.rank) if shard_bh else (0, BH)
+    bh = b1 - b0
+    tdt = {vc.Dtype.F16: torch.float16, vc.Dtype.BF16: torch.bfloat16, vc.Dtype.F32: torch.float32}[dtype]
+    g = torch.Generator(device="cuda").manual_seed(3 + dist.rank)
+    amp = 0.5 if dtype == vc.Dtype.BF16 else 1.0
+    Q, K, V = ((torch.randn(bh, N, d, device="cuda", generator=g) * amp).to(tdt) for _ in range(3))
+    O = torch.empty_like(Q)
+    scale = LOG2E / math.sqrt(d)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        check(vc.flash_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), bh, N, d, scale,
+                           causal, dtype, stream.cuda_stream), "vc_flash_fwd")
+
+    step()
+    torch.cuda.synchronize()
+    # parity guard: 32 rows of the last slice against torch fp32 SDPA
+    q = Q[-1:].float()
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q[:, -32:], K[-1:].float(), V[-1:].float(), is_causal=False,
+        attn_mask=(torch.arange(N, device="cuda")[None, :] <= torch.arange(N - 32, N, device="cuda")[:, None])
+        if causal else None)
+    perr = (O[-1:, -32:].float() - ref).abs().max().item()
+    tol = {vc.Dtype.F16: 2e-3, vc.Dtype.BF16: 1e-2, vc.Dtype.F32: 1e-4}[dtype]
+    if not perr <= tol:
+        raise RuntimeError(f"{name} parity guard failed: {perr}")
+    ms = timed(dist, stream, step, steps, warmup)
+    flop = (2.0 if causal else 4.0) * BH * N * N * d  # whole job
+    per_launch = ms / steps
+    value = flop / (per_launch * 1e-3) / 1e12 if shard_bh else flop * dist.world / (per_launch * 1e-3) / 1e12
+    local_flop = (2.0 if causal else 4.0) * bh * N * N * d
+    achieved = local_flop / (per_launch * 1e-3) / 1e12
+    long_kernel = per_launch > 10.0
+    peak = pk["bf16_sustained"] if long_kernel else pk["bf16"]
+    res = {"workload": name, "value": round(value, 2), "unit": "TFLOP/s",
+           "ms_per_step": round(per_launch, 4),
+           "scaling": "strong" if shard_bh else "weak",
+           "config": {"B": B, "H": H, "N": N, "d": d, "causal": causal,
+                      "dtype": {1: "f16", 2: "bf16", 0: "f32"}[int(dtype)],
+                      "bh_per_rank": bh},
+           "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                        "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                        "peak_kind": ("bf16 dense sustained" if long_kernel else "bf16 dense burst")
+                        + f" ({pk['source']})",
+                        "traffic": traffic_table().get(name)},
+           "gpu_launches": steps, "parity_guard_max_err": perr}
+    if dtype == vc.Dtype.F32:
+        res["roofline"]["note"] = "fp32 CUDA-core path; latency bound at this size"
+    del Q, K, V, O
+    torch.cuda.empty_cache()
+    return res
+
+
+def stream_workload(vc, dist, steps, warmup, pk):
+    import torch
+    n_total = 1 << 30
+    b0, b1 = shard(n_total, dist.world, dist.rank)
+    n = b1 - b0
+    g = torch.Generator(device="cuda").manual_seed(5 + dist.rank)
+    a = torch.rand(n, device="cuda", generator=g)
+    b = torch.rand(n, device="cuda", generator=g)
+    c = torch.empty_like(a)
+    part = torch.zeros(1, dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream()
+    cs = stream.cuda_stream
+
+    def fused():
+        check(vc.vadd_sum_f32(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, part.data_ptr(), cs),
+              "vc_vadd_sum_f32")
+        if dist.pg:
+            dist.pg.all_reduce(part)
+
+    def vadd_only():
+        check(vc.vadd_f32(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, cs), "vc_vadd_f32")
+
+    def sum_only():
+        check(vc.sum_f32(c.data_ptr(), n, part.data_ptr(), cs), "vc_sum_f32")
+
+    fused()
+    torch.cuda.synchronize()
+    total = part.item()
+    # parity guard: fp64 sum of c on the device (torch) vs ours
+    ref = c.double().sum()
+    if dist.pg:
+        dist.pg.all_reduce(ref)
+    if not abs(total - ref.item()) <= 1e-6 * abs(ref.item()):
+        raise RuntimeError(f"stream parity guard failed: {total} vs {ref.item()}")
+    ms_fused = timed(dist, stream, fused, steps, warmup)
+    ms_vadd = timed(dist, stream, vadd_only, steps, warmup)
+    ms_sum = timed(dist, stream, sum_only, steps, warmup)
+    per = ms_fused / steps
+    gbs = 12.0 * n_total / (per * 1e-3) / 1e9
+    local_gbs = 12.0 * n / (per * 1e-3) / 1e9
+    vadd_gbs = 12.0 * n / (ms_vadd / steps * 1e-3) / 1e9
+    sum_gbs = 4.0 * n / (ms_sum / steps * 1e-3) / 1e9
+    pair_gbs = 16.0 * n / ((ms_vadd + ms_sum) / steps * 1e-3) / 1e9
+    res = {"workload": "stream", "value": round(gbs, 1), "unit": "GB/s",
+           "ms_per_step": round(per, 4), "scaling": "strong",
+           "config": {"n": n_total, "n_per_rank": n, "dtype": "f32",
+                      "step": "fused vadd+sum kernel, then NCCL all-reduce of the fp64 partial"},
+           "roofline": {"bound": "hbm", "achieved": round(local_gbs, 1), "peak": pk["hbm"],
+                        "unit": "GB/s", "frac": round(local_gbs / pk["hbm"], 4),
+                        "bytes_per_elem": 12, "traffic": traffic_table().get("stream_fused")},
+           "separate_kernels": {"vadd_gbs": round(vadd_gbs, 1), "sum_gbs": round(sum_gbs, 1),
+                                "pair_gbs_16B": round(pair_gbs, 1),
+                                "vadd_frac": round(vadd_gbs / pk["hbm"], 4),
+                                "sum_frac": round(sum_gbs / pk["hbm"], 4)},
+           "gpu_launches": steps, "sum_check_rel_err": abs(total - ref.item()) / abs(ref.item())}
+    del a, b, c
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_gemm_baseline(target_s=8.0):
+    """The oracle's fp64 GEMM (the demos' host reference loop) on a bounded
+    sample of C's rows, all host threads; TFLOP/s extrapolated per row."""
+    from oracle import oracle
+    N = GEMM_N
+    rng = np.random.default_rng(7)
+    a = (rng.random((N, N), dtype=np.float32) * 2 - 1).astype(np.float16).astype(np.float32)
+    b = (rng.random((N, N), dtype=np.float32) * 2 - 1).astype(np.float16).astype(np.float32)
+    threads = oracle.max_threads()
+    rows = max(2, threads)
+    t0 = time.perf_counter()
+    oracle.gemm(a, b, N, N, N, N, N, True, rows=(0, rows), threads=threads)
+    dt = time.perf_counter() - t0
+    rows2 = int(min(N, max(rows, rows * target_s / max(dt, 1e-3))))
+    t0 = time.perf_counter()
+    oracle.gemm(a, b, N, N, N, N, N, True, rows=(0, rows2), threads=threads)
+    dt2 = time.perf_counter() - t0
+    tflops = 2.0 * rows2 * N * N / dt2 / 1e12
+    return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows2} of {N} rows of C = A*B (4096^3 fp16 inputs), fp64 loop "
+                      f"(matmul_coopmat_bench.vc:171-176 form), {dt2:.1f} s",
+            "seconds": round(dt2, 2)}
+
+
+# ---------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--only", default="gemm,fa_causal,fa_bf16,stream,fa_f32")
+    args = ap.parse_args()
+    dist = Dist()
+    if args.warmup < 3:
+        args.warmup = 3  # timing rule: at least 3 warm-up steps
+
+    config = {"workload": "gemm_f16_4096x4096x4096_fp32out", "M": GEMM_N, "N": GEMM_N,
+              "K": GEMM_N, "layout": "row-major A[M][K], B[K][N], C[M][N]",
+              "gemms_per_step": GEMMS_PER_STEP,
+              "l2": f"inputs rotate over {ROTATE} buffer sets (512 MiB > 126 MB L2)",
+              "parallelism": f"weak: {dist.world} rank(s), one 4096-row block each"}
+
+    if args.impl == "reference":
+        if dist.rank != 0:
+            return
+        base = cpu_gemm_baseline()
+        line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "TFLOP/s",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(2.0 * GEMM_N ** 3 * GEMMS_PER_STEP / (base["value"] * 1e12) * 1e3, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f64", "data": "synthetic", "config": config, "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    torch.cuda.set_device(dist.local)
+    dist.init()
+    from vkcuda_b200 import vc
+    check(vc.vcInit(), "vcInit")
+    check(vc.vcSetDevice(dist.local), "vcSetDevice")
+    pk = peaks()
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dist.local).uuid)
+    only = set(args.only.split(","))
+
+    head = gemm_workload(vc, dist, args.steps, args.warmup, pk, uuid) if "gemm" in only else None
+    also = []
+    jobs = [("fa_causal", lambda: flash_workload(vc, dist, "fa_causal", 8, 16, 4096, 128, True,
+                                                 vc.Dtype.F16, max(args.steps, 10), args.warmup, pk,
+                                                 shard_bh=False)),
+            ("fa_bf16", lambda: flash_workload(vc, dist, "fa_bf16", 32, 32, 8192, 128, False,
+                                               vc.Dtype.BF16, max(3, min(args.steps, 5)),
+                                               args.warmup, pk, shard_bh=True)),
+            ("stream", lambda: stream_workload(vc, dist, max(args.steps, 10), args.warmup, pk)),
+            ("fa_f32", lambda: flash_workload(vc, dist, "fa_f32", 1, 1, 256, 64, False,
+                                              vc.Dtype.F32, max(args.steps, 20), args.warmup, pk,
+                                              shard_bh=False))]
+    for name, fn in jobs:
+        if name in only:
+            try:
+                also.append(fn())
+            except Exception as e:  # report, keep the headline
+                also.append({"workload": name, "error": f"{type(e).__name__}: {e}"})
+    kerr = vc.kernel_error(True)
+
+    if dist.rank == 0:
+        base = cpu_gemm_baseline() if head else None
+        line = {"metric": METRIC, "value": head["value"] if head else None, "unit": "TFLOP/s",
+                "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": head["ms_per_step"] if head else None,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f16", "data": "synthetic (seeded U[-1,1) fp16 inputs)",
+                "config": config}
+        if head:
+            for key in ("roofline", "clocks", "e2e", "gpu_launches", "per_launch_ms"):
+                line[key] = head[key]
+            line["cpu_baseline"] = base
+        line["also"] = also
+        line["device_error_word"] = kerr
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

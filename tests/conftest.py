@@ -1,0 +1,126 @@
+"""Shared fixtures. Tests marked `gpu` need a CUDA device (B200); the rest run
+on CPU. GPU tests talk to the kernels only through the C ABI of
+libVCRuntime.so (vkcuda_b200.vc) and check them against the CPU oracle."""
+from __future__ import annotations
+
+import ctypes
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (runs on the B200 box)")
+
+
+def _ensure_built():
+    from vkcuda_b200 import vc
+    if not os.path.exists(vc.LIB_PATH):
+        from vkcuda_b200 import build
+        build.build()
+    from oracle import oracle
+    if not os.path.exists(oracle.LIB_PATH):
+        oracle.build()
+
+
+@pytest.fixture(scope="session")
+def vc():
+    _ensure_built()
+    from vkcuda_b200 import vc as _vc
+    _vc.library()
+    return _vc
+
+
+@pytest.fixture(scope="session")
+def orc():
+    _ensure_built()
+    from oracle import oracle
+    return oracle
+
+
+@pytest.fixture(scope="session")
+def gpu(vc):
+    """Initialised runtime on a real GPU; fails (does not skip) without one."""
+    err = vc.vcInit()
+    assert err == vc.VCError.Success, f"vcInit failed: {err!r} (no CUDA device?)"
+    assert vc.vcSetDevice(0) == vc.VCError.Success
+    yield vc
+    assert vc.kernel_error(True) == 0, "a kernel left a device error code"
+
+
+class Dev:
+    """A device buffer owned by the test (vcMalloc / vcFree)."""
+
+    def __init__(self, vc, nbytes: int):
+        self.vc = vc
+        err, self.ptr = vc.vcMalloc(nbytes)
+        assert err == vc.VCError.Success, err
+        self.nbytes = nbytes
+
+    @classmethod
+    def from_host(cls, vc, arr: np.ndarray) -> "Dev":
+        arr = np.ascontiguousarray(arr)
+        d = cls(vc, max(arr.nbytes, 1))
+        if arr.nbytes:
+            assert vc.vcMemcpy(d.ptr, arr, arr.nbytes, vc.VCMemcpyKind.HostToDevice) == 0
+        return d
+
+    def to_host(self, dtype, count: int) -> np.ndarray:
+        out = np.empty(count, dtype)
+        if out.nbytes:
+            assert self.vc.vcMemcpy(out, self.ptr, out.nbytes, self.vc.VCMemcpyKind.DeviceToHost) == 0
+        return out
+
+    def free(self):
+        if self.ptr:
+            assert self.vc.vcFree(self.ptr) == 0
+            self.ptr = 0
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+@pytest.fixture
+def dev(gpu):
+    made = []
+
+    class _F:
+        @staticmethod
+        def alloc(nbytes):
+            d = Dev(gpu, nbytes)
+            made.append(d)
+            return d
+
+        @staticmethod
+        def put(arr):
+            d = Dev.from_host(gpu, arr)
+            made.append(d)
+            return d
+
+    yield _F
+    for d in made:
+        d.free()
+
+
+def to_half_bits(x: np.ndarray, bf16: bool):
+    """Round fp32 values to fp16/bf16 (RNE). Returns (raw uint16 bits, values
+    widened back to fp32)."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+    h = t.to(torch.bfloat16 if bf16 else torch.float16)
+    return h.view(torch.int16).numpy().view(np.uint16).copy(), h.float().numpy()
+
+
+def half_bits_to_f32(bits: np.ndarray, bf16: bool) -> np.ndarray:
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16))
+    return t.view(torch.bfloat16 if bf16 else torch.float16).float().numpy()

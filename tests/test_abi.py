@@ -1,0 +1,126 @@
+"""libVCRuntime.so on CPU: it loads without a GPU, exports every symbol the
+headers declare, and the host-side logic (error codes, kernel registry,
+argument checks, fault injection) behaves as the reference API specifies."""
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_c_symbols():
+    text = open(os.path.join(ROOT, "include", "vc_b200.h")).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char \*)\s*(vc_\w+)\(", text, re.M)))
+
+
+def _declared_cpp_functions():
+    text = open(os.path.join(ROOT, "include", "vc", "Runtime", "VCRuntime.h")).read()
+    return sorted(set(re.findall(r"^(?:VCError|const char \*)\s*(vc\w+)\(", text, re.M)))
+
+
+def _exported(lib_path, demangle):
+    cmd = ["nm", "-D", "--defined-only"] + (["-C"] if demangle else []) + [lib_path]
+    return subprocess.run(cmd, capture_output=True, text=True, check=True).stdout
+
+
+def test_library_loads_and_exports_c_abi(vc):
+    syms = _declared_c_symbols()
+    assert len(syms) >= 59
+    out = _exported(vc.LIB_PATH, False)
+    exported = set(re.findall(r" T (vc_\w+)$", out, re.M))
+    missing = [s for s in syms if s not in exported]
+    assert not missing, missing
+    # ...and the Python mirror binds exactly those.
+    assert set(vc.SIGNATURES) == set(syms)
+
+
+def test_library_exports_cpp_api(vc):
+    out = _exported(vc.LIB_PATH, True)
+    missing = [f for f in _declared_cpp_functions() if f"vc::{f}(" not in out]
+    assert not missing, missing
+
+
+def test_error_strings(vc):
+    assert vc.vcErrorString(vc.VCError.Success) == "success"
+    assert vc.vcErrorString(vc.VCError.InvalidKernel) == "invalid kernel"
+    assert vc.vcErrorString(vc.VCError.NotReady) == "not ready"
+    assert vc.vcErrorString(99) == "unknown error"
+
+
+def _no_gpu():
+    import torch
+    return not torch.cuda.is_available()
+
+
+@pytest.mark.skipif(not _no_gpu(), reason="checks the no-device behaviour")
+def test_no_device_behaviour(vc):
+    # vcGetDeviceCount initialises lazily and reports 0 devices with Success
+    # when initialisation fails (reference VCRuntime.cpp:5037-5047).
+    assert vc.vcGetDeviceCount() == (vc.VCError.Success, 0)
+    assert vc.vcInit() == vc.VCError.InitializationError
+    assert vc.vcSetDevice(0) == vc.VCError.InitializationError
+    assert vc.vcGetDevice()[0] == vc.VCError.InitializationError
+    err, p = vc.vcMalloc(64)
+    assert err == vc.VCError.InitializationError and p == 0
+
+
+def test_kernel_registry_host_logic(vc):
+    for name in ["flashAttn", "wmma_gemm", "matmulCoopmat", "matmulTiled", "vadd", "blockReduce",
+                 "vc.gemm", "vc.flash_fwd", "vc.vadd", "vc.sum", "vc.vadd_sum",
+                 "vc.block_reduce"]:
+        err, k = vc.vcLoadKernel(None, name)
+        assert err == vc.VCError.Success and k, name
+        assert vc.vcReleaseKernel(k) == vc.VCError.Success
+    # SPIR-V magic is checked when a module is given.
+    assert vc.vcLoadKernel([0x07230203, 0, 0], "vadd")[0] == vc.VCError.Success
+    assert vc.vcLoadKernel([0xdeadbeef], "vadd")[0] == vc.VCError.InvalidKernel
+    assert vc.vcLoadKernel(None, "noSuchKernel")[0] == vc.VCError.InvalidKernel
+    assert vc.vcLoadKernel([0x07230203, 1], "main")[0] == vc.VCError.InvalidKernel
+    err, k = vc.vcLoadKernel(None, "flashAttn")
+    assert vc.vcKernelSetConstant(k, "SEQ", 128) == vc.VCError.Success
+    assert vc.vcKernelSetConstant(k, "NOPE", 1) == vc.VCError.InvalidValue
+    assert vc.vcKernelSetConstant(k, "SEQ", 0) == vc.VCError.InvalidValue
+    vc.vcReleaseKernel(k)
+
+
+def test_launch_argument_checks(vc):
+    # Null kernel -> InvalidKernel; zero block -> InvalidValue (both before
+    # any device work, as in the reference wrappers VCRuntime.cpp:5584-5609).
+    assert vc.vcLaunchKernel(None, 64, 32, []) == vc.VCError.InvalidKernel
+    err, k = vc.vcLoadKernel(None, "vadd")
+    assert vc.vcLaunchKernel(k, 64, 0, []) == vc.VCError.InvalidValue
+    vc.vcReleaseKernel(k)
+    assert vc.vcMemcpy(None, None, 4, vc.VCMemcpyKind.HostToDevice) == vc.VCError.InvalidValue
+    assert vc.vcMemset(None, 0, 4) == vc.VCError.InvalidValue
+    assert vc.vcFree(None) == vc.VCError.Success
+    assert vc.vcMemcpy2DAsync(1, 4, 1, 4, 4, 1, vc.VCMemcpyKind.HostToDevice) == vc.VCError.InvalidValue
+
+
+def _run_child(code: str, env_extra: dict) -> str:
+    env = dict(os.environ, **env_extra)
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
+                         cwd=ROOT, timeout=120)
+    assert res.returncode == 0, res.stderr
+    return res.stdout.strip()
+
+
+def test_fault_injection_malloc_and_launch():
+    # The 2nd vcMalloc and the 1st launch fail with the injected codes, before
+    # any device is touched (host-side failure injection, no GPU needed).
+    out = _run_child(
+        "from vkcuda_b200 import vc\n"
+        "a = int(vc.vcMalloc(16)[0]); b = int(vc.vcMalloc(16)[0]); c = int(vc.vcMalloc(16)[0])\n"
+        "k = vc.vcLoadKernel(None, 'vadd')[1]\n"
+        "l1 = int(vc.vcLaunchKernel(k, 64, 32, [])); l2 = int(vc.vcLaunchKernel(k, 64, 32, []))\n"
+        "print(a, b, c, l1, l2)\n",
+        {"VC_FAULT_INJECT": "malloc:2,launch:1"})
+    a, b, c, l1, l2 = (int(x) for x in out.split())
+    assert b == 2                      # OutOfMemory injected on call 2
+    assert a == c and a in (0, 5)      # real result: Success on a GPU, InitializationError on CPU
+    assert l1 == 8                     # Unknown injected on launch 1
+    assert l2 != 8

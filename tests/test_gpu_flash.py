@@ -1,0 +1,136 @@
+"""Flash-attention forward on the GPU through the C ABI against the fp64
+oracle (the reference's referenceAttn restated).
+Bars: fp32 path <= 1e-4 absolute (the demo's own check, flash_attn.vc:230-236);
+fp16 path <= 2e-3 and bf16 path <= 1e-2 absolute (fp64 softmax over the
+rounded inputs)."""
+from __future__ import annotations
+
+import math
+import os
+import struct
+
+import numpy as np
+import pytest
+
+from conftest import half_bits_to_f32, to_half_bits
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TOL = {"f32": 1e-4, "f16": 2e-3, "bf16": 1e-2}
+LOG2E = 1.4426950408889634
+
+
+def load_vcfa(path):
+    raw = open(path, "rb").read()
+    nh, seq, hd, causal = (int(v) for v in struct.unpack("<4f", raw[4:20]))
+    body = np.frombuffer(raw[20:], "<f4")
+    e = nh * seq * hd
+    return (nh, seq, hd, causal), [body[i * e:(i + 1) * e].copy() for i in range(5)]
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_flash_attn_demo_legacy_launch(gpu, dev, causal):
+    """examples/flash_attn.vc end to end: its inputs, its launch
+    (grid NHEAD*SEQ elements, block BR), its scale and its 1e-4 check against
+    the reference's host output stored in the golden fixture."""
+    (nh, seq, hd, c), (Q, K, V, _, O_host) = load_vcfa(
+        os.path.join(GOLDEN, f"fa_demo_causal{causal}.bin"))
+    dq, dk, dv, do = dev.put(Q), dev.put(K), dev.put(V), dev.alloc(Q.nbytes)
+    err, k = gpu.vcLoadKernel(None, "flashAttn")
+    scale = np.float32(LOG2E / math.sqrt(hd))
+    assert gpu.vcLaunchKernel(k, nh * seq, 16, [gpu.ptr(dq.ptr), gpu.ptr(dk.ptr), gpu.ptr(dv.ptr),
+                                                gpu.ptr(do.ptr), gpu.f32(scale),
+                                                gpu.i32(causal)]) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    assert np.abs(do.to_host(np.float32, Q.size) - O_host).max() <= TOL["f32"]
+    gpu.vcReleaseKernel(k)
+
+
+def test_flash_attn_legacy_constants(gpu, dev, orc):
+    """NHEAD/SEQ/HDIM are compile-time in the demo; vcKernelSetConstant sets them."""
+    nh, seq, hd = 3, 96, 32
+    Q, K, V = orc.fa_inputs(99, nh * seq * hd)
+    scale = np.float32(LOG2E / math.sqrt(hd))
+    dq, dk, dv, do = dev.put(Q), dev.put(K), dev.put(V), dev.alloc(Q.nbytes)
+    err, k = gpu.vcLoadKernel(None, "flashAttn")
+    for name, v in (("NHEAD", nh), ("SEQ", seq), ("HDIM", hd)):
+        assert gpu.vcKernelSetConstant(k, name, v) == 0
+    args = [gpu.ptr(dq.ptr), gpu.ptr(dk.ptr), gpu.ptr(dv.ptr), gpu.ptr(do.ptr), gpu.f32(scale),
+            gpu.i32(1)]
+    assert gpu.vcLaunchKernel(k, nh * seq, 16, args) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    ref = orc.attention(Q, K, V, nh, seq, hd, scale, True)
+    assert np.abs(do.to_host(np.float32, Q.size) - ref).max() <= TOL["f32"]
+    # A grid that does not match NHEAD*SEQ is refused.
+    assert gpu.vcLaunchKernel(k, 64, 16, args) == gpu.VCError.InvalidValue
+    gpu.vcReleaseKernel(k)
+
+
+@pytest.mark.parametrize("BH,N,d,causal", [(1, 256, 64, False), (2, 100, 16, True),
+                                           (3, 333, 128, False), (2, 64, 32, True)])
+def test_flash_f32_vs_oracle(gpu, dev, orc, BH, N, d, causal):
+    rng = np.random.default_rng(BH * N + d)
+    Q, K, V = (rng.standard_normal(BH * N * d).astype(np.float32) for _ in range(3))
+    s = np.float32(LOG2E / math.sqrt(d))
+    dq, dk, dv, do = dev.put(Q), dev.put(K), dev.put(V), dev.alloc(Q.nbytes)
+    assert gpu.flash_fwd(dq.ptr, dk.ptr, dv.ptr, do.ptr, BH, N, d, s, causal, gpu.Dtype.F32) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    ref = orc.attention(Q, K, V, BH, N, d, s, causal)
+    assert np.abs(do.to_host(np.float32, Q.size) - ref).max() <= TOL["f32"]
+
+
+def _run_tc(gpu, dev, orc, BH, N, d, causal, bf16, seed=0, scale_in=1.0, bh_check=None,
+            row_check=None):
+    rng = np.random.default_rng(seed)
+    raw = [(rng.standard_normal(BH * N * d) * scale_in).astype(np.float32) for _ in range(3)]
+    bits, vals = zip(*(to_half_bits(x, bf16) for x in raw))
+    s = np.float32(LOG2E / math.sqrt(d))
+    dq, dk, dv = (dev.put(b) for b in bits)
+    do = dev.alloc(BH * N * d * 2)
+    dt = gpu.Dtype.BF16 if bf16 else gpu.Dtype.F16
+    err = gpu.flash_fwd(dq.ptr, dk.ptr, dv.ptr, do.ptr, BH, N, d, s, causal, dt)
+    assert err == 0, err
+    assert gpu.vcDeviceSynchronize() == 0
+    assert gpu.kernel_error(True) == 0
+    got = half_bits_to_f32(do.to_host(np.uint16, BH * N * d), bf16).reshape(BH, N, d)
+    ref = orc.attention(*vals, BH, N, d, s, causal, bh_range=bh_check,
+                        row_range=row_check).reshape(BH, N, d)
+    b0, b1 = bh_check or (0, BH)
+    r0, r1 = row_check or (0, N)
+    err = np.abs(got[b0:b1, r0:r1] - ref[b0:b1, r0:r1]).max()
+    assert np.isfinite(got).all()
+    assert err <= TOL["bf16" if bf16 else "f16"], err
+    return got
+
+
+@pytest.mark.parametrize("BH,N,d,causal", [(2, 128, 128, False), (2, 128, 128, True),
+                                           (3, 512, 128, True), (2, 200, 128, False),
+                                           (2, 333, 64, True), (1, 1024, 64, False),
+                                           (4, 1, 128, True), (1, 640, 128, False)])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_flash_tcgen05_vs_oracle(gpu, dev, orc, BH, N, d, causal, bf16):
+    _run_tc(gpu, dev, orc, BH, N, d, causal, bf16, seed=BH + N + d + causal,
+            scale_in=0.5 if bf16 else 1.0)
+
+
+def test_flash_tcgen05_large_scores_rescale(gpu, dev, orc):
+    # Inputs scaled x4 give scores spanning hundreds of log2 units: exercises
+    # the conditional rescale of O (max growing by more than 2^8 mid-row).
+    _run_tc(gpu, dev, orc, 2, 512, 128, False, False, seed=3, scale_in=4.0)
+
+
+def test_flash_tcgen05_config3_sampled(gpu, dev, orc):
+    """Benchmark config: fp16, B=8, H=16, N=4096, d=128, causal; rows checked
+    on a sample (4 slices x 64 rows, including the last rows of the sequence)."""
+    _run_tc(gpu, dev, orc, 128, 4096, 128, True, False, seed=3, bh_check=(60, 64),
+            row_check=(4032, 4096))
+
+
+def test_flash_rejects_bad_shapes(gpu, dev):
+    d = dev.alloc(1 << 16)
+    # head dim 96 has no tensor-core path
+    assert gpu.flash_fwd(d.ptr, d.ptr, d.ptr, d.ptr, 1, 64, 96, 0.1, False, gpu.Dtype.F16) \
+        == gpu.VCError.InvalidValue
+    # buffers smaller than BH*N*d are refused before launch
+    assert gpu.flash_fwd(d.ptr, d.ptr, d.ptr, d.ptr, 8, 4096, 128, 0.1, False, gpu.Dtype.F16) \
+        == gpu.VCError.InvalidValue

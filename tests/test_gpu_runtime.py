@@ -1,0 +1,156 @@
+"""Runtime API semantics on the GPU, mirroring the reference's runtime demos
+(test/event.vc, test/profiling.vc, test/stream_query.vc, test/graph.vc,
+test/multigpu.vc): allocation registry, blocking vs async copies, memset
+rules, streams, events and elapsed time, graph record/replay, host callbacks,
+peer copies, and the bounded-wait failure path."""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_device_properties(gpu):
+    err, n = gpu.vcGetDeviceCount()
+    assert err == 0 and n >= 1
+    err, p = gpu.vcGetDeviceProperties(0)
+    assert err == 0
+    assert p.multiProcessorCount >= 100 and p.warpSize == 32 and p.major >= 10
+    assert gpu.vcGetDeviceProperties(n)[0] == gpu.VCError.InvalidDevice
+    assert gpu.vcSetDevice(n) == gpu.VCError.InvalidDevice
+    assert gpu.vcGetDevice() == (gpu.VCError.Success, 0)
+
+
+def test_pointer_attributes_and_free(gpu):
+    err, d = gpu.vcMalloc(4096)
+    err2, h = gpu.vcMallocHost(1024)
+    assert err == 0 and err2 == 0
+    e, a = gpu.vcPointerGetAttributes(d)
+    assert e == 0 and a.memoryType == gpu.VCMemoryType.Device and a.size == 4096
+    e, a = gpu.vcPointerGetAttributes(d + 100)  # interior pointer
+    assert a.memoryType == gpu.VCMemoryType.Device and a.devicePointer == d
+    e, a = gpu.vcPointerGetAttributes(h)
+    assert a.memoryType == gpu.VCMemoryType.Host and a.hostPointer == h
+    stack = ctypes.c_int(0)
+    e, a = gpu.vcPointerGetAttributes(ctypes.addressof(stack))
+    assert a.memoryType == gpu.VCMemoryType.Unregistered and a.size == 0
+    assert gpu.vcFree(d) == 0 and gpu.vcFree(h) == 0
+    e, a = gpu.vcPointerGetAttributes(d)
+    assert a.memoryType == gpu.VCMemoryType.Unregistered
+    assert gpu.vcFree(d) == gpu.VCError.InvalidValue  # no longer a VC allocation
+
+
+def test_copies_and_memset(gpu, dev):
+    x = np.arange(1024, dtype=np.int32)
+    d1, d2 = dev.put(x), dev.alloc(4096)
+    assert gpu.vcMemcpy(d2.ptr, d1.ptr, 4096, gpu.VCMemcpyKind.DeviceToDevice) == 0
+    assert np.array_equal(d2.to_host(np.int32, 1024), x)
+    assert gpu.vcMemset(d2.ptr, 0x01, 4096) == 0
+    assert (d2.to_host(np.int32, 1024) == 0x01010101).all()
+    assert gpu.vcMemset(d2.ptr, 0, 6) == gpu.VCError.InvalidValue       # count % 4
+    assert gpu.vcMemset(d2.ptr, 0, 8192) == gpu.VCError.InvalidValue    # past the allocation
+    # 2D pitched copy: 4 rows of 16 bytes from pitch 64 to pitch 32.
+    assert gpu.vcMemcpy2DAsync(d2.ptr, 32, d1.ptr, 64, 16, 4, gpu.VCMemcpyKind.DeviceToDevice) == 0
+    gpu.vcStreamSynchronize(None)
+    got = d2.to_host(np.int32, 32).reshape(4, 8)[:, :4]
+    assert np.array_equal(got, x.reshape(-1, 16)[:4, :4])
+    assert gpu.vcMemset2DAsync(d2.ptr, 32, 0, 16, 4) == 0
+    gpu.vcStreamSynchronize(None)
+    assert (d2.to_host(np.int32, 32).reshape(4, 8)[:, :4] == 0).all()
+
+
+def test_async_copy_stream_and_events(gpu, dev):
+    n = 1 << 22
+    x = np.random.default_rng(0).random(n, dtype=np.float32)
+    err, hbuf = gpu.vcMallocHost(x.nbytes)
+    ctypes.memmove(hbuf, x.ctypes.data, x.nbytes)
+    d = dev.alloc(x.nbytes)
+    err, s = gpu.vcStreamCreate()
+    err, e0 = gpu.vcEventCreate()
+    err, e1 = gpu.vcEventCreate()
+    # Elapsed time of never-recorded events is InvalidValue (reference contract).
+    assert gpu.vcEventElapsedTime(e0, e1)[0] == gpu.VCError.InvalidValue
+    assert gpu.vcEventRecord(e0, s) == 0
+    assert gpu.vcMemcpyAsyncS(d.ptr, hbuf, x.nbytes, gpu.VCMemcpyKind.HostToDevice, s) == 0
+    assert gpu.vcEventRecord(e1, s) == 0
+    assert gpu.vcEventSynchronize(e1) == 0
+    err, done = gpu.vcEventQuery(e1)
+    assert err == 0 and done == 1
+    err, ms = gpu.vcEventElapsedTime(e0, e1)
+    assert err == 0 and ms > 0.0
+    err, done = gpu.vcStreamQuery(s)
+    assert done == 1
+    # Cross-stream dependency: default stream waits on e1 before reading.
+    assert gpu.vcStreamWaitEvent(None, e1) == 0
+    assert np.array_equal(d.to_host(np.float32, n), x)
+    for e in (e0, e1):
+        gpu.vcEventDestroy(e)
+    gpu.vcStreamDestroy(s)
+    gpu.vcFree(hbuf)
+
+
+def test_graph_record_replay(gpu, dev, orc):
+    n = 100_000
+    rng = np.random.default_rng(4)
+    a = rng.random(n, dtype=np.float32)
+    b = rng.random(n, dtype=np.float32)
+    da, db, dc = dev.put(a), dev.put(b), dev.alloc(4 * n)
+    err, k = gpu.vcLoadKernel(None, "vadd")
+    err, g = gpu.vcGraphCreate()
+    assert gpu.vcGraphBeginRecord(g) == 0
+    assert gpu.vcLaunchKernel(k, n, 256, [gpu.ptr(da.ptr), gpu.ptr(db.ptr), gpu.ptr(dc.ptr),
+                                          gpu.i32(n)]) == 0
+    # The recorded launch reads c back into a: a <- a + b on every replay.
+    assert gpu.vcMemcpyAsync(da.ptr, dc.ptr, 4 * n, gpu.VCMemcpyKind.DeviceToDevice) == 0
+    assert gpu.vcGraphEndRecord(g) == 0
+    ref = a.copy()
+    for _ in range(3):
+        assert gpu.vcGraphLaunch(g, None) == 0
+        ref = orc.vadd(ref, b)
+    assert gpu.vcStreamSynchronize(None) == 0
+    assert np.array_equal(da.to_host(np.float32, n), ref)
+    assert gpu.vcGraphReset(g) == 0
+    assert gpu.vcGraphLaunch(g, None) == gpu.VCError.InvalidValue  # reset graphs are empty
+    gpu.vcGraphDestroy(g)
+    gpu.vcReleaseKernel(k)
+
+
+def test_host_func_runs_after_stream_work(gpu, dev):
+    fired = threading.Event()
+    seen = []
+
+    def cb(_user):
+        seen.append(1)
+        fired.set()
+
+    d = dev.alloc(1 << 20)
+    assert gpu.vcMemsetAsyncS(d.ptr, 0, 1 << 20, None) == 0
+    assert gpu.vcLaunchHostFunc(None, cb) == 0
+    assert fired.wait(10.0) and seen == [1]
+
+
+def test_peer_copy_same_device(gpu, dev):
+    """test/multigpu.vc degrades to a 0 -> 0 peer copy on one device."""
+    x = 1000 + np.arange(1024, dtype=np.int32)
+    src, dst = dev.put(x), dev.alloc(4096)
+    assert gpu.vcMemcpyPeer(dst.ptr, 0, src.ptr, 0, 4096) == 0
+    assert np.array_equal(dst.to_host(np.int32, 1024), x)
+    err, n = gpu.vcGetDeviceCount()
+    assert gpu.vcMemcpyPeer(dst.ptr, n, src.ptr, 0, 4096) == gpu.VCError.InvalidDevice
+    assert gpu.vcMemcpyPeer(dst.ptr, 0, src.ptr, 0, 8192) == gpu.VCError.InvalidValue
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(gpu, dev, orc):
+    # A device wait on a barrier nothing arrives on gives up after ~2 ms and
+    # reports its code (3); the context stays usable afterwards.
+    assert gpu.selftest_bounded_wait(2000) == 3
+    a = np.ones(1000, np.float32)
+    da, dc = dev.put(a), dev.alloc(4000)
+    assert gpu.vadd_f32(da.ptr, da.ptr, dc.ptr, 1000) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    assert (dc.to_host(np.float32, 1000) == 2.0).all()
+    assert gpu.kernel_error(True) == 0

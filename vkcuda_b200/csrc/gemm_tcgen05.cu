@@ -1,0 +1,326 @@
+// gemm_tcgen05.cu - D[M][N] (fp32) = A[M][K] * B (+ Cin) on sm_100a tensor
+// cores; fp16 or bf16 inputs, fp32 accumulation.
+//
+// Replaces the cooperative-matrix GEMMs of the reference demos:
+// test/wmma_gemm.vc:19-33 (one 8x8x16 tile, D = A*B + C) and
+// examples/matmul_coopmat_bench.vc:60-110 (16x16 tiles of 2x2 8x8x16 MMAs,
+// accumulator streamed through global C every K step).
+//
+// Design (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile 128x64 and B tile 64x256 (or 256x64)
+//               per stage, 128-byte swizzled, 4-stage ring (48 KiB/stage).
+//   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma
+//               (M=128, N=256, K=16, fp32 accumulator in TMEM), commits each
+//               stage back to the producer and each finished tile to the
+//               epilogue. Two accumulators (2 x 256 columns) alternate, so
+//               the MMAs of tile i+1 overlap the epilogue of tile i.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns per thread-row, optional
+//               Cin addend, swizzled staging in shared memory (2 x 16 KiB),
+//               TMA store of 128x32 fp32 boxes.
+// Ragged M, N and K are handled by TMA: loads zero-fill outside the matrix
+// and stores clip, so any shape whose row strides meet TMA's 16-byte rule
+// runs here. Roofline: 2*M*N*K FLOP against the dense fp16/bf16 tensor peak.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace vcb {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
+constexpr int kStages = 4;
+constexpr int kAccCols = BN;
+constexpr uint32_t kTmemCols = 2 * kAccCols;  // 512: two accumulators
+constexpr int kEpiCols = 32;
+constexpr uint32_t kABytes = BM * BK * 2;
+constexpr uint32_t kBBytes = BN * BK * 2;
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kEpiBytes = BM * kEpiCols * 4;
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+
+struct __align__(8) GemmBarriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+constexpr size_t kSmemBytes =
+    1024 /* alignment slack */ + kStages * kStageBytes + 2 * kEpiBytes + sizeof(GemmBarriers);
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmD,
+                    const float *__restrict__ Cin, int64_t ldc, int M, int N, int K,
+                    uint32_t idesc, int b_kn) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *stage_base = smem;
+  uint8_t *epi_base = smem + kStages * kStageBytes;
+  GemmBarriers *bars = reinterpret_cast<GemmBarriers *>(epi_base + 2 * kEpiBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (M + BM - 1) / BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], kEpiThreads);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmD);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int tm = tile / tiles_n, tn = tile % tiles_n;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bars->empty[stage], phase ^ 1u)) { ok = false; break; }
+          uint8_t *sA = stage_base + stage * kStageBytes;
+          uint8_t *sB = sA + kABytes;
+          mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
+          tma_load_2d(sA, &tmA, kb * BK, tm * BM, &bars->full[stage]);
+          if (b_kn) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + j * (64 * BK * 2), &tmB, tn * BN + j * 64, kb * BK,
+                          &bars->full[stage]);
+          } else {
+            tma_load_2d(sB, &tmB, kb * BK, tn * BN, &bars->full[stage]);
+          }
+          ++issued;
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: every issued load must land before the CTA may exit (only
+      // matters when a wait above gave up; otherwise these pass at once).
+      const uint32_t last = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
+      for (uint32_t i = 0; i < last; ++i) {
+        const uint32_t idx = issued - 1 - i;
+        mbar_wait(&bars->full[idx % kStages], (idx / kStages) & 1u, 1000000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kAccCols;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bars->full[stage], phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(stage_base + stage * kStageBytes);
+          const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc =
+                b_kn ? smem_desc_sw128(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
+                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&bars->empty[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit(&bars->acc_full[acc]);
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, thread = accumulator row
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const int etid = threadIdx.x - 64;
+    uint8_t *row_stage[2] = {epi_base + row * 128, epi_base + kEpiBytes + row * 128};
+    int local = 0;
+    uint32_t chunk_count = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int tm = tile / tiles_n, tn = tile % tiles_n;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&bars->acc_full[acc], acc_phase)) break;
+      tc_fence_after();
+      const int m0 = tm * BM, n0 = tn * BN;
+      const int gr = m0 + row;
+      for (int c = 0; c < BN / kEpiCols; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * kAccCols + c * kEpiCols, v);
+        tmem_ld_wait();
+        if (c == BN / kEpiCols - 1) {
+          tc_fence_before();
+          mbar_arrive(&bars->acc_empty[acc]);
+        }
+        const int cn0 = n0 + c * kEpiCols;
+        if (cn0 >= N) continue;  // tile-uniform: whole box right of the matrix
+        if (Cin != nullptr && gr < M) {
+          const float *crow = Cin + (int64_t)gr * ldc;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (cn0 + j < N) v[j] = __float_as_uint(__uint_as_float(v[j]) + crow[cn0 + j]);
+        }
+        const int buf = chunk_count & 1;
+        if (etid == 0) bulk_wait_group_read<1>();
+        named_bar_sync(1, kEpiThreads);
+        uint8_t *dst = row_stage[buf];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int phys = j ^ (row & 7);  // 128-byte swizzle of 16-byte chunks
+          *reinterpret_cast<uint4 *>(dst + phys * 16) =
+              make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, kEpiThreads);
+        if (etid == 0) {
+          tma_store_2d(&tmD, epi_base + buf * kEpiBytes, cn0, m0);
+          bulk_commit_group();
+        }
+        ++chunk_count;
+      }
+    }
+    if (etid == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t,
+                                  void *, const cuuint64_t *, const cuuint64_t *,
+                                  const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+bool make_map_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes,
+                 const void *base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                 uint32_t box_inner, uint32_t box_outer) {
+  auto encode = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!encode) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, type, 2, const_cast<void *>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct MapCache {
+  GemmArgs key{};
+  int device = -1;
+  CUtensorMap a, b, d;
+  bool valid = false;
+};
+
+bool same_key(const GemmArgs &x, const GemmArgs &y) {
+  return x.A == y.A && x.B == y.B && x.D == y.D && x.M == y.M && x.N == y.N &&
+         x.K == y.K && x.lda == y.lda && x.ldb == y.ldb && x.ldd == y.ldd &&
+         x.bf16 == y.bf16 && x.b_kn == y.b_kn;
+}
+
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return cudaErrorInvalidValue;
+  // TMA rules: 16-byte aligned bases, row strides multiples of 16 bytes.
+  if (!al16(g.A) || !al16(g.B) || !al16(g.D)) return cudaErrorNotSupported;
+  if (g.lda % 8 || g.ldb % 8 || g.ldd % 4) return cudaErrorNotSupported;
+  if (g.lda < g.K || g.ldd < g.N) return cudaErrorInvalidValue;
+  if (g.b_kn ? g.ldb < g.N : g.ldb < g.K) return cudaErrorInvalidValue;
+  if (g.Cin && g.ldc < g.N) return cudaErrorInvalidValue;
+
+  static thread_local MapCache cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(cache.valid && cache.device == dev && same_key(cache.key, g))) {
+    const CUtensorMapDataType t16 =
+        g.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    bool ok = make_map_2d(&cache.a, t16, 2, g.A, g.K, g.M, g.lda, BK, BM);
+    if (g.b_kn)
+      ok = ok && make_map_2d(&cache.b, t16, 2, g.B, g.N, g.K, g.ldb, 64, BK);
+    else
+      ok = ok && make_map_2d(&cache.b, t16, 2, g.B, g.K, g.N, g.ldb, BK, BN);
+    ok = ok && make_map_2d(&cache.d, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.D, g.N, g.M,
+                           g.ldd, kEpiCols, BM);
+    if (!ok) {
+      cache.valid = false;
+      return cudaErrorNotSupported;
+    }
+    cache.key = g;
+    cache.device = dev;
+    cache.valid = true;
+  }
+
+  static int configured_device_mask = 0;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(configured_device_mask & (1 << dev))) {
+      cudaError_t e = cudaFuncSetAttribute(gemm_tcgen05_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kSmemBytes);
+      if (e != cudaSuccess) return e;
+      configured_device_mask |= (1 << dev);
+    }
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+  const int grid = tiles < sms ? tiles : sms;
+  const uint32_t idesc = idesc_f16_f32(BM, BN, g.bf16, false, g.b_kn);
+  gemm_tcgen05_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
+      cache.a, cache.b, cache.d, g.Cin, g.ldc, g.M, g.N, g.K, idesc, g.b_kn ? 1 : 0);
+  return cudaGetLastError();
+}
+
+}  // namespace vcb
+
+VCB_DEFINE_ERROR_ACCESSOR(gemm_tcgen05_error)

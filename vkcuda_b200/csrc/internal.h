@@ -1,0 +1,71 @@
+// internal.h - host-side launchers of the sm_100a kernels, shared by the
+// runtime (registry adapters) and the flat C ABI. All return cudaError_t;
+// shape errors that the kernels cannot serve come back as
+// cudaErrorInvalidValue before anything is launched.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace vcb {
+
+// ---- streaming (stream_kernels.cu)
+int stream_max_blocks();
+cudaError_t launch_vadd_f32(const float *a, const float *b, float *c, int64_t n,
+                            cudaStream_t stream);
+// Sum of x (or of c = x + b written out when b != nullptr) into *out (device
+// double). `partials` holds >= max_blocks doubles and `ticket` one zeroed
+// unsigned int; both are left ready for the next call.
+cudaError_t launch_sum_f32(const float *x, const float *b, float *c, int64_t n,
+                           double *out, double *partials, unsigned int *ticket,
+                           int max_blocks, cudaStream_t stream);
+cudaError_t launch_block_reduce_demo(const float *in, float *out, int n, int block,
+                                     int groups, cudaStream_t stream);
+
+// ---- GEMM (gemm_tcgen05.cu, gemm_simt.cu)
+struct GemmArgs {
+  const void *A;      // [M][K] row-major, stride lda elements
+  const void *B;      // b_kn ? [K][N] (stride ldb) : [N][K] (stride ldb)
+  float *D;           // [M][N] fp32, stride ldd
+  const float *Cin;   // optional [M][N] fp32 addend, stride ldc
+  int M, N, K;
+  int64_t lda, ldb, ldd, ldc;
+  bool bf16;          // element type of A and B (fp16 otherwise)
+  bool b_kn;          // B stored K-rows x N-columns
+};
+// tcgen05 path; cudaErrorNotSupported when the strides / alignment do not
+// meet its TMA requirements (then the caller uses the SIMT path).
+cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream);
+cudaError_t launch_gemm_simt(const GemmArgs &g, cudaStream_t stream);
+// fp32 SIMT C = A * B (the reference's matmulTiled, fp32 in and out).
+cudaError_t launch_matmul_f32(const float *A, const float *B, float *C, int M, int N,
+                              int K, int64_t lda, int64_t ldb, int64_t ldc,
+                              cudaStream_t stream);
+
+// ---- flash attention (flash_fwd_tcgen05.cu, flash_fwd_f32.cu)
+struct FlashArgs {
+  const void *Q, *K, *V;
+  void *O;
+  int BH, N, d;
+  float scale_log2;  // scores * scale_log2 are exponentiated in base 2
+  bool causal;
+  int dtype;         // 0 f32, 1 f16, 2 bf16
+};
+cudaError_t launch_flash_fwd_tcgen05(const FlashArgs &f, cudaStream_t stream);
+cudaError_t launch_flash_fwd_f32(const FlashArgs &f, cudaStream_t stream);
+
+// ---- device error words, one accessor per translation unit
+int stream_kernels_error(int clear);
+int gemm_tcgen05_error(int clear);
+int flash_tcgen05_error(int clear);
+int selftest_error(int clear);
+cudaError_t launch_selftest_bounded_wait(unsigned timeout_us, cudaStream_t stream);
+
+// ---- runtime-owned scratch (runtime.cpp): per (device, stream) partials
+// buffer and ticket for the reductions. Never freed before vcShutdown.
+cudaError_t reduce_scratch(cudaStream_t stream, double **partials,
+                           unsigned int **ticket, int *capacity);
+
+// Driver entry point for tensor-map encoding (fetched once via the runtime).
+void *tensor_map_encoder();
+
+}  // namespace vcb

@@ -1,0 +1,311 @@
+// stream_kernels.cu - the bandwidth-bound half of the hot path on sm_100a:
+//   * vadd:       c = a + b                         (test/vadd.vc:12-17)
+//   * sum:        one fp64 scalar = sum of x         (test/reduce.vc scaled up)
+//   * vadd_sum:   c = a + b and sum(c) in one pass   (both, fused: 12 B/elem)
+//   * block reduce with the reference's exact pairing (test/reduce.vc:11-38)
+//
+// Layout and roofline: flat fp32 arrays in HBM. The vector kernels move
+// 16-byte vectors with streaming cache hints, keep 4 vectors per operand in
+// flight per thread, and run a grid of (resident CTAs x 148 SMs) so every SM
+// has enough bytes in flight to cover HBM latency. Algorithmic traffic:
+// vadd 12 B/elem, sum 4 B/elem, vadd_sum 12 B/elem.
+//
+// Summation order: each thread adds runs of up to 16 elements in fp32 and
+// folds each run into an fp64 accumulator; warps and blocks combine in fp64;
+// block partials land in a scratch array and the last block to finish adds
+// them in index order. The result is deterministic for a given grid.
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace vcb {
+namespace {
+
+constexpr int kStreamThreads = 512;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ float4 ld_stream(const float4 *p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream(float4 *p, float4 v) { __stcs(p, v); }
+
+__device__ __forceinline__ float4 add4(float4 x, float4 y) {
+  return make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+}
+__device__ __forceinline__ float hsum4(float4 v) { return (v.x + v.y) + (v.z + v.w); }
+
+// c[i] = a[i] + b[i] over n4 float4 vectors, grid-stride, 4 vectors per
+// thread per trip.
+__global__ void __launch_bounds__(kStreamThreads)
+vadd_vec_kernel(const float4 *__restrict__ a, const float4 *__restrict__ b,
+                float4 *__restrict__ c, int64_t n4) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
+    float4 va[kUnroll], vb[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      va[u] = ld_stream(a + i + u * stride);
+      vb[u] = ld_stream(b + i + u * stride);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) st_stream(c + i + u * stride, add4(va[u], vb[u]));
+  }
+  for (; i < n4; i += stride) st_stream(c + i, add4(ld_stream(a + i), ld_stream(b + i)));
+}
+
+// Scalar form for the tail (n % 4) and for unaligned pointers.
+__global__ void vadd_scalar_kernel(const float *__restrict__ a,
+                                   const float *__restrict__ b,
+                                   float *__restrict__ c, int64_t begin,
+                                   int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = begin + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < n; i += stride)
+    c[i] = a[i] + b[i];
+}
+
+// Block-wide fp64 sum; result valid in thread 0.
+__device__ __forceinline__ double block_sum_f64(double v, double *red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    t = lane < nw ? red[lane] : 0.0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) t += __shfl_down_sync(0xffffffffu, t, off);
+  }
+  return t;
+}
+
+// Last-block-done combine: block partials -> *out in index order; the ticket
+// counter is reset so the scratch is ready for the next launch.
+__device__ __forceinline__ void combine_partials(double block_total, double *partials,
+                                                 unsigned int *ticket, double *out,
+                                                 double *red) {
+  __shared__ bool is_last;
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = block_total;
+    __threadfence();
+    const unsigned int done = atomicAdd(ticket, 1u);
+    is_last = (done == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // Fixed-order combine: thread t sums partials t, t+blockDim, ...; then the
+  // block tree (fixed shape) adds those.
+  double v = 0.0;
+  for (unsigned int i = threadIdx.x; i < gridDim.x; i += blockDim.x)
+    v += static_cast<volatile double *>(partials)[i];
+  __syncthreads();
+  const double total = block_sum_f64(v, red);
+  if (threadIdx.x == 0) {
+    *out = total;
+    *ticket = 0u;
+  }
+}
+
+// sum(x) with optional fused vadd: when `b` is non-null, c = x + b is written
+// and summed; otherwise x itself is summed (c unused).
+template <bool kFused>
+__global__ void __launch_bounds__(kStreamThreads)
+sum_vec_kernel(const float4 *__restrict__ x, const float4 *__restrict__ b,
+               float4 *__restrict__ c, int64_t n4, const float *__restrict__ xs,
+               const float *__restrict__ bs, float *__restrict__ cs,
+               int64_t n, double *partials, unsigned int *ticket,
+               double *out) {
+  __shared__ double red[kStreamThreads / 32];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  double acc = 0.0;
+  int64_t i = tid;
+  for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      v[u] = ld_stream(x + i + u * stride);
+      if (kFused) v[u] = add4(v[u], ld_stream(b + i + u * stride));
+    }
+    float run = 0.0f;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (kFused) st_stream(c + i + u * stride, v[u]);
+      run += hsum4(v[u]);
+    }
+    acc += static_cast<double>(run);
+  }
+  for (; i < n4; i += stride) {
+    float4 v = ld_stream(x + i);
+    if (kFused) {
+      v = add4(v, ld_stream(b + i));
+      st_stream(c + i, v);
+    }
+    acc += static_cast<double>(hsum4(v));
+  }
+  // Scalar tail (n not a multiple of 4): elements [4*n4, n).
+  for (int64_t j = 4 * n4 + tid; j < n; j += stride) {
+    float v = xs[j];
+    if (kFused) {
+      v = v + bs[j];
+      cs[j] = v;
+    }
+    acc += static_cast<double>(v);
+  }
+  const double total = block_sum_f64(acc, red);
+  __syncthreads();
+  combine_partials(total, partials, ticket, out, red);
+}
+
+// Scalar-pointer form of sum for inputs that are not 16-byte aligned.
+template <bool kFused>
+__global__ void __launch_bounds__(kStreamThreads)
+sum_scalar_kernel(const float *__restrict__ x, const float *__restrict__ b,
+                  float *__restrict__ c, int64_t n, double *partials,
+                  unsigned int *ticket, double *out) {
+  __shared__ double red[kStreamThreads / 32];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  double acc = 0.0;
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < n;
+       j += stride) {
+    float v = x[j];
+    if (kFused) {
+      v = v + b[j];
+      c[j] = v;
+    }
+    acc += static_cast<double>(v);
+  }
+  const double total = block_sum_f64(acc, red);
+  __syncthreads();
+  combine_partials(total, partials, ticket, out, red);
+}
+
+// Demo block reduce. The pairing follows the reference tree exactly: with
+// s = block/2, block/4, ..., 1 (integer halving), slot t < s takes slot t + s.
+// Levels with s > 16 go through shared memory; the last levels (every live
+// slot then below 32) run as warp shuffles inside warp 0, which pair the same
+// slots (lane t reads lane t + s, and slots >= s are never written at that
+// level), so each partial is bit-identical to the reference for any block
+// size, power of two or not.
+__global__ void block_reduce_demo_kernel(const float *__restrict__ in,
+                                         float *__restrict__ out, int n,
+                                         int block) {
+  extern __shared__ float slots[];
+  const int t = threadIdx.x;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * block + t;
+  slots[t] = (t < block && i < n) ? in[i] : 0.0f;
+  __syncthreads();
+  int s = block / 2;
+  // Shared-memory levels until every slot that can still contribute
+  // (index < 2s) lies inside warp 0, i.e. s <= 16.
+  for (; s > 16; s /= 2) {
+    if (t < s) slots[t] = slots[t] + slots[t + s];
+    __syncthreads();
+  }
+  if (t < 32) {
+    // Lanes >= block hold no slot; a lane t < s only reads lane t + s < 2s,
+    // and 2s <= 32 here.
+    float v = (t < block) ? slots[t] : 0.0f;
+    for (; s > 0; s /= 2) {
+      const float other = __shfl_down_sync(0xffffffffu, v, s);
+      if (t < s) v = v + other;
+    }
+    if (t == 0) out[blockIdx.x] = v;
+  }
+}
+
+__global__ void fill_f64_kernel(double *p, double v) { *p = v; }
+
+int stream_grid(int64_t work_items) {
+  static int sm_count = 0;
+  if (sm_count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (sm_count <= 0) sm_count = 148;
+  }
+  // Four resident 512-thread CTAs per SM (2048 threads) keep ~128 KiB in
+  // flight per SM; fewer CTAs when the array is small.
+  const int64_t full = static_cast<int64_t>(sm_count) * 4;
+  const int64_t need = (work_items + kStreamThreads - 1) / kStreamThreads;
+  int64_t g = need < full ? need : full;
+  return g < 1 ? 1 : static_cast<int>(g);
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int stream_max_blocks() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms * 4;
+}
+
+cudaError_t launch_vadd_f32(const float *a, const float *b, float *c, int64_t n,
+                            cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  if (aligned16(a) && aligned16(b) && aligned16(c)) {
+    const int64_t n4 = n / 4;
+    if (n4 > 0) {
+      vadd_vec_kernel<<<stream_grid(n4 / kUnroll + 1), kStreamThreads, 0, stream>>>(
+          reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b),
+          reinterpret_cast<float4 *>(c), n4);
+    }
+    if (n % 4)
+      vadd_scalar_kernel<<<1, 32, 0, stream>>>(a, b, c, n4 * 4, n);
+  } else {
+    vadd_scalar_kernel<<<stream_grid(n / kUnroll + 1), kStreamThreads, 0, stream>>>(
+        a, b, c, 0, n);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sum_f32(const float *x, const float *b, float *c, int64_t n,
+                           double *out, double *partials, unsigned int *ticket,
+                           int max_blocks, cudaStream_t stream) {
+  if (n < 0) return cudaErrorInvalidValue;
+  const bool fused = (b != nullptr);
+  const bool vec = aligned16(x) && (!fused || (aligned16(b) && aligned16(c)));
+  const int64_t units = vec ? (n / 4) / kUnroll + 1 : n / kUnroll + 1;
+  int grid = stream_grid(units);
+  if (grid > max_blocks) grid = max_blocks;
+  if (vec) {
+    const int64_t n4 = n / 4;
+    if (fused)
+      sum_vec_kernel<true><<<grid, kStreamThreads, 0, stream>>>(
+          reinterpret_cast<const float4 *>(x), reinterpret_cast<const float4 *>(b),
+          reinterpret_cast<float4 *>(c), n4, x, b, c, n, partials, ticket, out);
+    else
+      sum_vec_kernel<false><<<grid, kStreamThreads, 0, stream>>>(
+          reinterpret_cast<const float4 *>(x), nullptr, nullptr, n4, x, nullptr,
+          nullptr, n, partials, ticket, out);
+  } else {
+    if (fused)
+      sum_scalar_kernel<true><<<grid, kStreamThreads, 0, stream>>>(x, b, c, n, partials,
+                                                                   ticket, out);
+    else
+      sum_scalar_kernel<false><<<grid, kStreamThreads, 0, stream>>>(
+          x, nullptr, nullptr, n, partials, ticket, out);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_block_reduce_demo(const float *in, float *out, int n, int block,
+                                     int groups, cudaStream_t stream) {
+  if (block <= 0 || block > 1024 || groups <= 0) return cudaErrorInvalidValue;
+  // Threads: at least one warp so the shuffle levels have 32 lanes.
+  const int threads = block < 32 ? 32 : ((block + 31) / 32) * 32;
+  block_reduce_demo_kernel<<<groups, threads, threads * sizeof(float), stream>>>(
+      in, out, n, block);
+  return cudaGetLastError();
+}
+
+}  // namespace vcb
+
+VCB_DEFINE_ERROR_ACCESSOR(stream_kernels_error)
