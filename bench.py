@@ -42,12 +42,17 @@ sys.path.insert(0, ROOT)
 
 METRIC = "attn-fwd & GEMM TFLOP/s (% of B200 dense peak), reduce GB/s, at 1/2/4/8 GPU"
 GEMM_N = 4096
-GEMMS_PER_STEP = 100
+GEMMS_PER_STEP = 400
 ROTATE = 4
 LOG2E = 1.4426950408889634
 
 
 # ---------------------------------------------------------------- helpers
+def set_gemms_per_step(n: int) -> None:
+    global GEMMS_PER_STEP
+    GEMMS_PER_STEP = max(1, int(n))
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -65,7 +70,7 @@ def traffic_table():
 
 
 class ClockSampler:
-    """nvidia-smi samples (every 100 ms) while the timed region runs."""
+    """nvidia-smi samples (every 50 ms) while the timed region runs."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -80,7 +85,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -466,7 +471,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--only", default="gemm,fa_causal,fa_bf16,stream,fa_f32")
+    ap.add_argument("--gemms-per-step", type=int, default=GEMMS_PER_STEP,
+                    help="GEMM products per step (small values for profiler captures)")
     args = ap.parse_args()
+    set_gemms_per_step(args.gemms_per_step)
     dist = Dist()
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps

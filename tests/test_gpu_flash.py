@@ -80,9 +80,10 @@ def test_flash_f32_vs_oracle(gpu, dev, orc, BH, N, d, causal):
 
 
 def _run_tc(gpu, dev, orc, BH, N, d, causal, bf16, seed=0, scale_in=1.0, bh_check=None,
-            row_check=None):
+            row_check=None, qk_scale=1.0):
     rng = np.random.default_rng(seed)
-    raw = [(rng.standard_normal(BH * N * d) * scale_in).astype(np.float32) for _ in range(3)]
+    raw = [(rng.standard_normal(BH * N * d) * scale_in * (qk_scale if i < 2 else 1.0))
+           .astype(np.float32) for i in range(3)]
     bits, vals = zip(*(to_half_bits(x, bf16) for x in raw))
     s = np.float32(LOG2E / math.sqrt(d))
     dq, dk, dv = (dev.put(b) for b in bits)
@@ -114,9 +115,11 @@ def test_flash_tcgen05_vs_oracle(gpu, dev, orc, BH, N, d, causal, bf16):
 
 
 def test_flash_tcgen05_large_scores_rescale(gpu, dev, orc):
-    # Inputs scaled x4 give scores spanning hundreds of log2 units: exercises
+    # Q and K scaled x4 give scores spanning hundreds of log2 units: exercises
     # the conditional rescale of O (max growing by more than 2^8 mid-row).
-    _run_tc(gpu, dev, orc, 2, 512, 128, False, False, seed=3, scale_in=4.0)
+    # V keeps unit variance, so the absolute bar keeps its meaning.
+    _run_tc(gpu, dev, orc, 2, 512, 128, False, False, seed=3, qk_scale=4.0)
+    _run_tc(gpu, dev, orc, 2, 512, 128, True, True, seed=4, qk_scale=4.0)
 
 
 def test_flash_tcgen05_config3_sampled(gpu, dev, orc):

@@ -8,26 +8,36 @@
 // alpha = exp2(m_old - m_new), p = exp2(s - m), O = acc / l), optionally
 // causal (key j > query i masked, flash_attn.vc:100).
 //
-// Design, per CTA (one 128-row query tile of one slice; 2 CTAs per SM so one
-// CTA's MMAs overlap the other's softmax):
-//   TMEM (256 columns): S = Q K^T (128 x 128 fp32) in columns [0,128); the
-//     probabilities P are written back as 16-bit pairs over S columns
-//     [0,64); O (128 x d fp32) lives in columns [128, 128+d).
-//   warp 4      TMA producer: Q once, then per key tile K and V (128 rows x
-//               d, 128-byte swizzled 64-column boxes), one buffer each.
-//   warp 5      allocates TMEM; lane 0 issues S = Q K^T (A and B from shared
-//               memory, both K-major) and O += P V (A = P from TMEM, B = V
-//               from shared memory, d-contiguous = MN-major).
-//   warps 0..3  softmax, thread = query row: row max from S, conditional
-//               rescale of O (only when a row max grows by more than 2^8,
-//               which keeps p <= 256 and is exact after the final 1/l),
-//               P = exp2(s * scale_log2 - m) packed to 16 bits into TMEM,
-//               row sum l in fp32; at the end O / l is staged in shared
-//               memory and stored with TMA.
-// Causal tiles above the diagonal are skipped; keys >= N in the last tile
-// and keys above the diagonal in the diagonal tile are masked.
-// Roofline: 4*BH*N^2*d FLOP (half of that causal) against the dense tensor
-// peak.
+// Design: one CTA per SM, 320 threads, two 128-row query tiles (Q0, Q1) of
+// one slice per CTA, 128-key K/V tiles.
+//   TMEM (512 columns): S0 = Q0 K^T at [0,128), S1 at [128,256), O0 at
+//     [256,384), O1 at [384,512), fp32. The probabilities P_w are written
+//     back as 16-bit pairs over the first 64 columns of S_w.
+//   warp 8      TMA producer: Q0 and Q1 once; K(j), V(j) alternately into a
+//               4-stage ring of 128-row, 128-byte-swizzled tiles.
+//   warp 9      allocates TMEM; lane 0 issues the MMAs in the order
+//                 S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) ...
+//               (S_w = Q_w K^T: A and B K-major in shared memory; PV_w:
+//               A = P_w from TMEM, B = V d-contiguous = MN-major), so the
+//               softmax of one tile overlaps the MMAs of the other. A commit
+//               after S_w(j) also covers PV_w(j-1), so when softmax w sees
+//               S_w(j) its O_w is stable and may be rescaled in place.
+//   warps 0..3  softmax of Q0 (thread = row = TMEM lane), warps 4..7 of Q1:
+//               the whole 128-column S row is loaded into registers with one
+//               TMEM wait (a measured 2.5x faster than two waits on halves),
+//               row max, conditional rescale of O (only when the max grows
+//               by more than 2^8; p <= 256 otherwise and the final 1/l makes
+//               it exact), P = exp2(scale_log2 * s - m) rounded to 16 bits,
+//               row sum of the rounded P (numerator and denominator use the
+//               same weights). One exponential in four runs as a polynomial
+//               on the FMA pipe, which relieves the MUFU unit (16 ex2 per
+//               clock per SM against 8192 MMA FLOP per clock). At the end O / l is staged over the Q tile and
+//               stored with TMA.
+// Causal: Q0 of query block b uses key tiles 0..2b, Q1 0..2b+1; blocks are
+// scheduled heaviest first. Keys >= N and keys above the diagonal are masked.
+// Grid: query blocks of one slice are adjacent, so the slices in flight (and
+// their K/V) stay within L2.
+// Roofline: 4*BH*N^2*d FLOP (2*BH*N^2*d causal) against the dense tensor peak.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -41,34 +51,35 @@
 namespace vcb {
 namespace {
 
-constexpr int BQ = 128;    // query rows per CTA
+constexpr int BQ = 128;    // query rows per tile (two tiles per CTA)
 constexpr int BKV = 128;   // keys per tile
-constexpr int kThreads = 192;
-constexpr int kSoftmaxThreads = 128;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kSCol = 0;    // S / P columns
-constexpr uint32_t kOCol = 128;  // O columns
+constexpr int kStages = 4; // K/V ring depth
+constexpr int kThreads = 320;  // 10 warps: 168 registers per thread at most
+                               // (3 warps share one SM sub-partition's 16K)
+constexpr int kWgThreads = 128;
+constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kBoxBytes = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct __align__(8) FlashBarriers {
   uint64_t q_full;
-  uint64_t k_full, k_empty;
-  uint64_t v_full, v_empty;
-  uint64_t s_full, p_full, o_full;
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_full[2];
   uint32_t tmem_base;
 };
 
 template <int HD>
 struct FlashSmem {
-  static constexpr uint32_t kTileBytes = (HD / 64) * kBoxBytes;  // Q, K or V tile
-  static constexpr uint32_t kQ = 0, kK = kTileBytes, kV = 2 * kTileBytes;
-  static constexpr uint32_t kBars = 3 * kTileBytes;
-  // Requested dynamic shared memory: the tiles, the barriers and alignment
-  // slack, raised to ~100 KiB so at most two CTAs share an SM (their two
-  // 256-column TMEM allocations fill the SM's 512 columns exactly).
+  static constexpr uint32_t kTile = (HD / 64) * kBoxBytes;  // one Q, K or V tile
+  static constexpr uint32_t kQ0 = 0, kQ1 = kTile, kRing = 2 * kTile;
+  static constexpr uint32_t kBars = kRing + kStages * kTile;
   static constexpr size_t kUsed = 1024 + kBars + sizeof(FlashBarriers);
-  static constexpr size_t kRequest = kUsed > 100 * 1024 ? kUsed : 100 * 1024;
+  // At least 120 KiB so that a second CTA never shares the SM: each CTA
+  // allocates all 512 TMEM columns.
+  static constexpr size_t kBytes = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
 };
 
 template <bool BF16>
@@ -82,8 +93,36 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+// Sum of the two 16-bit values of a packed pair, in fp32.
+template <bool BF16>
+__device__ __forceinline__ float sum2(uint32_t w) {
+  if constexpr (BF16) {
+    return __uint_as_float(w << 16) + __uint_as_float(w & 0xffff0000u);
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
+    return f.x + f.y;
+  }
+}
+
+// 2^x on the FMA pipe: x = i + f with i = round(x) (the 1.5 * 2^23 shifter
+// leaves round(x) in the low mantissa bits), f in [-0.5, 0.5]; 2^f by a
+// degree-3 polynomial fitted here to 2^f on that interval (iterated weighted
+// least squares on Chebyshev nodes, max relative error 7.5e-5, below the
+// 16-bit rounding of P); 2^i by adding i to the exponent field. Inputs below
+// -126 (including -inf for masked scores) return exactly 0, like the ftz
+// MUFU exponential.
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float shifter = 12582912.0f;
+  const float t = xc + shifter;
+  const float f = xc - (t - shifter);
+  const float p = fmaf(fmaf(fmaf(0.055171654f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
+  const int i = __float_as_int(t) - __float_as_int(shifter);
+  return x < -126.0f ? 0.0f : __int_as_float(__float_as_int(p) + (i << 23));
+}
+
 template <int HD, bool BF16>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                  const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV,
@@ -93,31 +132,32 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sQ = smem + L::kQ;
-  uint8_t *sK = smem + L::kK;
-  uint8_t *sV = smem + L::kV;
   FlashBarriers *bars = reinterpret_cast<FlashBarriers *>(smem + L::kBars);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
-  const int num_qt = (N + BQ - 1) / BQ;
-  const int qt = num_qt - 1 - blockIdx.y;  // heaviest causal tiles first
-  const int kv_tiles_all = (N + BKV - 1) / BKV;
-  const int nkv = causal ? min(qt + 1, kv_tiles_all) : kv_tiles_all;
+  const int nqb = (N + 2 * BQ - 1) / (2 * BQ);
+  const int qb = causal ? (nqb - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+  const int bh = blockIdx.y;
+  const int kv_all = (N + BKV - 1) / BKV;
+  // Key tiles used by Q0 / Q1 (n1 >= n0).
+  const int n0 = causal ? min(2 * qb + 1, kv_all) : kv_all;
+  const int n1 = causal ? min(2 * qb + 2, kv_all) : kv_all;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    mbar_init(&bars->k_full, 1);
-    mbar_init(&bars->k_empty, 1);
-    mbar_init(&bars->v_full, 1);
-    mbar_init(&bars->v_empty, 1);
-    mbar_init(&bars->s_full, 1);
-    mbar_init(&bars->p_full, kSoftmaxThreads);
-    mbar_init(&bars->o_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->kv_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&bars->s_full[w], 1);
+      mbar_init(&bars->p_full[w], kWgThreads);
+      mbar_init(&bars->o_full[w], 1);
+    }
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
@@ -126,180 +166,221 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(&bars->q_full, L::kTileBytes);
+      mbar_arrive_expect_tx(&bars->q_full, 2 * L::kTile);
 #pragma unroll
-      for (int c = 0; c < HD / 64; ++c)
-        tma_load_3d(sQ + c * kBoxBytes, &tmQ, c * 64, qt * BQ, bh, &bars->q_full);
-      int k_loads = 0, v_loads = 0;
-      for (int j = 0; j < nkv; ++j) {
-        if (j > 0 && !mbar_wait(&bars->k_empty, (j - 1) & 1)) break;
-        mbar_arrive_expect_tx(&bars->k_full, L::kTileBytes);
-#pragma unroll
-        for (int c = 0; c < HD / 64; ++c)
-          tma_load_3d(sK + c * kBoxBytes, &tmK, c * 64, j * BKV, bh, &bars->k_full);
-        ++k_loads;
-        if (j > 0 && !mbar_wait(&bars->v_empty, (j - 1) & 1)) break;
-        mbar_arrive_expect_tx(&bars->v_full, L::kTileBytes);
-#pragma unroll
-        for (int c = 0; c < HD / 64; ++c)
-          tma_load_3d(sV + c * kBoxBytes, &tmV, c * 64, j * BKV, bh, &bars->v_full);
-        ++v_loads;
+      for (int c = 0; c < HD / 64; ++c) {
+        tma_load_3d(smem + L::kQ0 + c * kBoxBytes, &tmQ, c * 64, qb * 2 * BQ, bh, &bars->q_full);
+        tma_load_3d(smem + L::kQ1 + c * kBoxBytes, &tmQ, c * 64, qb * 2 * BQ + BQ, bh,
+                    &bars->q_full);
       }
-      // Drain the last loads before the CTA may exit (immediate unless a
-      // wait gave up).
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < n1; ++j) {
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv) {
+          const uint32_t idx = 2 * j + kv;
+          const int st = idx % kStages;
+          if (!mbar_wait(&bars->kv_empty[st], ((idx / kStages) & 1u) ^ 1u)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->kv_full[st], L::kTile);
+          const CUtensorMap *map = kv ? &tmV : &tmK;
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_3d(smem + L::kRing + st * L::kTile + c * kBoxBytes, map, c * 64, j * BKV, bh,
+                        &bars->kv_full[st]);
+          ++issued;
+        }
+      }
       mbar_wait(&bars->q_full, 0, 1000000000ull);
-      if (k_loads) mbar_wait(&bars->k_full, (k_loads - 1) & 1, 1000000000ull);
-      if (v_loads) mbar_wait(&bars->v_full, (v_loads - 1) & 1, 1000000000ull);
+      const uint32_t last = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
+      for (uint32_t i = 0; i < last; ++i) {
+        const uint32_t idx = issued - 1 - i;
+        mbar_wait(&bars->kv_full[idx % kStages], (idx / kStages) & 1u, 1000000000ull);
+      }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
       const uint32_t idesc_s = idesc_f16_f32(BQ, BKV, BF16, false, false);
       const uint32_t idesc_o = idesc_f16_f32(BQ, HD, BF16, false, true);
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      bool ok = mbar_wait(&bars->q_full, 0);
-      for (int j = 0; ok && j < nkv; ++j) {
-        if (!mbar_wait(&bars->k_full, j & 1)) break;
-        tc_fence_after();
+      const uint32_t q_addr[2] = {smem_u32(smem + L::kQ0), smem_u32(smem + L::kQ1)};
+      const uint32_t ring = smem_u32(smem + L::kRing);
+      auto issue_s = [&](int w, uint32_t k_idx) {
+        const uint32_t kaddr = ring + (k_idx % kStages) * L::kTile;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
           const uint32_t off = (ks / 4) * kBoxBytes + (ks % 4) * 32;
-          mma_f16_ss(tmem + kSCol, smem_desc_sw128(q_addr + off, 16, 1024),
-                     smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
+          mma_f16_ss(tmem + w * 128, smem_desc_sw128(q_addr[w] + off, 16, 1024),
+                     smem_desc_sw128(kaddr + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
         }
-        mma_commit(&bars->k_empty);
-        mma_commit(&bars->s_full);
-        if (!mbar_wait(&bars->p_full, j & 1)) break;
-        tc_fence_after();
-        if (!mbar_wait(&bars->v_full, j & 1)) break;
-        tc_fence_after();
+        mma_commit(&bars->s_full[w]);
+      };
+      auto issue_pv = [&](int w, uint32_t v_idx, bool accumulate) {
+        const uint32_t vaddr = ring + (v_idx % kStages) * L::kTile;
 #pragma unroll
-        for (int ks = 0; ks < BKV / 16; ++ks) {
-          mma_f16_ts(tmem + kOCol, tmem + kSCol + ks * 8,
-                     smem_desc_sw128(v_addr + ks * 16 * 128, kBoxBytes, 1024), idesc_o,
-                     (j > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 0; ks < BKV / 16; ++ks)
+          mma_f16_ts(tmem + 256 + w * 128, tmem + w * 128 + ks * 8,
+                     smem_desc_sw128(vaddr + ks * 16 * 128, kBoxBytes, 1024), idesc_o,
+                     (accumulate || ks > 0) ? 1u : 0u);
+        mma_commit(&bars->o_full[w]);
+      };
+      auto wait_full = [&](uint32_t idx) {
+        const bool ok = mbar_wait(&bars->kv_full[idx % kStages], (idx / kStages) & 1u);
+        tc_fence_after();
+        return ok;
+      };
+      bool ok = mbar_wait(&bars->q_full, 0) && wait_full(0);
+      if (ok) {
+        if (n0 > 0) issue_s(0, 0);
+        issue_s(1, 0);
+        mma_commit(&bars->kv_empty[0]);
+      }
+      for (int j = 0; ok && j < n1; ++j) {
+        const uint32_t v_idx = 2 * j + 1, k_next = 2 * j + 2;
+        if (!wait_full(v_idx)) break;
+        bool k_ready = false;
+        if (j < n0) {
+          if (!mbar_wait(&bars->p_full[0], j & 1)) break;
+          tc_fence_after();
+          issue_pv(0, v_idx, j > 0);
+          if (j + 1 < n0) {
+            if (!wait_full(k_next)) break;
+            k_ready = true;
+            issue_s(0, k_next);
+          }
         }
-        mma_commit(&bars->v_empty);
-        mma_commit(&bars->o_full);
+        if (!mbar_wait(&bars->p_full[1], j & 1)) break;
+        tc_fence_after();
+        issue_pv(1, v_idx, j > 0);
+        mma_commit(&bars->kv_empty[v_idx % kStages]);
+        if (j + 1 < n1) {
+          if (!k_ready && !wait_full(k_next)) break;
+          issue_s(1, k_next);
+          mma_commit(&bars->kv_empty[k_next % kStages]);
+        }
       }
     }
   } else {
-    // -------------------------------------------------- softmax, warps 0..3
-    const int row = warp * 32 + lane;  // == TMEM lane of this thread
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    const int qi = qt * BQ + row;
+    // -------------------------------------------------- softmax, warps 0..7
+    const int w = warp >> 2;              // which query tile
+    const int quad = warp & 3;            // TMEM lane quadrant
+    const int row = quad * 32 + lane;     // row within the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + w * 128;
+    const uint32_t o_col = tmem + lane_off + 256 + w * 128;
+    const int qi = qb * 2 * BQ + w * BQ + row;
+    const int nkv = w ? n1 : n0;
     float m_run = -INFINITY;  // running max of scale_log2 * s
     float l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait(&bars->s_full, j & 1)) { ok = false; break; }
+      if (!mbar_wait(&bars->s_full[w], j & 1)) { ok = false; }
       tc_fence_after();
       const int key0 = j * BKV;
-      const bool tail = (key0 + BKV > N);
-      const bool diag = causal && (j == nkv - 1);
-      const bool need_mask = tail || diag;
-      // Pass 1: row max.
+      const bool need_mask = (key0 + BKV > N) || (causal && key0 + BKV - 1 > qb * 2 * BQ + w * BQ);
+      // The whole S row in registers: four loads, one wait.
+      uint32_t s[BKV / 32][32];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) tmem_ld32(s_col + c * 32, s[c]);
+      tmem_ld_wait();
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < BKV / 32; ++c)
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            const int key = key0 + c * 32 + t;
+            if (key >= N || (causal && key > qi)) s[c][t] = __float_as_uint(-INFINITY);
+          }
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t s[32];
-        tmem_ld32(lane_base + kSCol + c * 32, s);
-        tmem_ld_wait();
+      for (int c = 0; c < BKV / 32; ++c)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int key = key0 + c * 32 + t;
-          const bool masked = need_mask && (key >= N || (causal && key > qi));
-          const float v = masked ? -INFINITY : __uint_as_float(s[t]);
-          mx = fmaxf(mx, v);
-        }
-      }
+        for (int t = 0; t < 32; ++t) mx = fmaxf(mx, __uint_as_float(s[c][t]));
       const float m_cand = fmaxf(m_run, mx * scale_log2);
-      const bool grow = m_cand > m_run + kRescaleThreshold;  // true on first tile
-      if (__any_sync(0xffffffffu, grow)) {
+      const bool grow = m_cand > m_run + kRescaleThreshold;  // true on the first tile
+      // Warp-uniform decision (TMEM loads and stores are warp-collective).
+      const bool rescale = __any_sync(0xffffffffu, grow);
+      float alpha = 1.0f;
+      if (rescale) {
         if (j > 0) {
-          // O holds PV of earlier tiles: wait for the last one, then rescale
-          // this warp's rows by exp2(m_run - m_cand).
-          if (!mbar_wait(&bars->o_full, (j - 1) & 1)) { ok = false; }
-          tc_fence_after();
-          const float alpha = (m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - m_cand);
+          alpha = ex2_approx(m_run - m_cand);
           l_run *= alpha;
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(lane_base + kOCol + c * 32, o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
-            tmem_st32(lane_base + kOCol + c * 32, o);
-          }
-          tmem_st_wait();
         }
         m_run = m_cand;
       }
       const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-      // Pass 2: P = exp2(scale_log2 * s - m) -> 16-bit pairs over S columns.
+      // P = exp2(scale_log2 * s - m) -> 16-bit pairs over S columns; one in
+      // four exponentials runs on the FMA pipe (exp2_poly) to offload MUFU.
+      // The row sum adds the rounded values.
       float lsum = 0.0f;
 #pragma unroll
       for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t s[32];
-        tmem_ld32(lane_base + kSCol + c * 32, s);
-        tmem_ld_wait();
         uint32_t p[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          const int key = key0 + c * 32 + 2 * t;
-          float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * t]), scale_log2, -m_use));
-          float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * t + 1]), scale_log2, -m_use));
-          if (need_mask) {
-            if (key >= N || (causal && key > qi)) p0 = 0.0f;
-            if (key + 1 >= N || (causal && key + 1 > qi)) p1 = 0.0f;
-          }
-          lsum += p0 + p1;
+          const float x0 = fmaf(__uint_as_float(s[c][2 * t]), scale_log2, -m_use);
+          const float x1 = fmaf(__uint_as_float(s[c][2 * t + 1]), scale_log2, -m_use);
+          // Masked scores are -inf: both exponentials return exactly 0.
+          const float p0 = ex2_approx(x0);
+          const float p1 = (t & 1) ? exp2_poly(x1) : ex2_approx(x1);
           p[t] = pack2<BF16>(p0, p1);
+          lsum += sum2<BF16>(p[t]);
         }
-        tmem_st16(lane_base + kSCol + c * 16, p);
+        tmem_st16(s_col + c * 16, p);
       }
       l_run += lsum;
+      if (rescale && j > 0) {
+        // S_w(j) complete implies PV_w(j-1) complete: O_w is stable. Done
+        // after P so that S is no longer live in registers.
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_col + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+          tmem_st32(o_col + c * 32, o);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->p_full);
+      mbar_arrive(&bars->p_full[w]);
       if (!ok) break;
     }
-    // Epilogue: O / l -> 16-bit, staged over the Q tile, TMA store.
-    if (ok && mbar_wait(&bars->o_full, (nkv - 1) & 1)) {
+    // Epilogue: O / l -> 16-bit, staged over this tile's Q buffer, TMA store.
+    if (ok && nkv > 0 && mbar_wait(&bars->o_full[w], (nkv - 1) & 1)) {
       tc_fence_after();
+      uint8_t *stage = smem + (w ? L::kQ1 : L::kQ0);
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
-        tmem_ld32(lane_base + kOCol + c * 32, o);
+        tmem_ld32(o_col + c * 32, o);
         tmem_ld_wait();
-        // 32 fp32 -> 16 packed words = 64 bytes = chunks 4*(c%2) .. +3 of
-        // the 128-byte row of box c/2.
-        uint8_t *rowp = sQ + (c / 2) * kBoxBytes + row * 128;
+        uint8_t *rowp = stage + (c / 2) * kBoxBytes + row * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint4 w;
-          w.x = pack2<BF16>(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
-          w.y = pack2<BF16>(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
-          w.z = pack2<BF16>(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
-          w.w = pack2<BF16>(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
+          uint4 v;
+          v.x = pack2<BF16>(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
+          v.y = pack2<BF16>(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
+          v.z = pack2<BF16>(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
+          v.w = pack2<BF16>(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
           const int chunk = (c % 2) * 4 + q;
-          *reinterpret_cast<uint4 *>(rowp + ((chunk ^ (row & 7)) * 16)) = w;
+          *reinterpret_cast<uint4 *>(rowp + ((chunk ^ (row & 7)) * 16)) = v;
         }
       }
       fence_proxy_async_smem();
-      named_bar_sync(1, kSoftmaxThreads);
-      if (threadIdx.x == 0) {
+      named_bar_sync(1 + w, kWgThreads);
+      if (quad == 0 && lane == 0) {
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c)
-          tma_store_3d(&tmO, sQ + c * kBoxBytes, c * 64, qt * BQ, bh);
+          tma_store_3d(&tmO, stage + c * kBoxBytes, c * 64, qb * 2 * BQ + w * BQ, bh);
         bulk_commit_group();
         bulk_wait_group<0>();
       }
@@ -309,7 +390,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 9) tmem_dealloc(tmem, kTmemCols);
 }
 
 // ------------------------------------------------------------ host side
@@ -345,13 +426,13 @@ cudaError_t launch_typed(const FlashArgs &f, const CUtensorMap &q, const CUtenso
     if (!(configured & (1 << dev))) {
       cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<HD, BF16>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)FlashSmem<HD>::kRequest);
+                                           (int)FlashSmem<HD>::kBytes);
       if (e != cudaSuccess) return e;
       configured |= (1 << dev);
     }
   }
-  dim3 grid(f.BH, (f.N + BQ - 1) / BQ);
-  flash_fwd_kernel<HD, BF16><<<grid, kThreads, FlashSmem<HD>::kRequest, stream>>>(
+  dim3 grid((f.N + 2 * BQ - 1) / (2 * BQ), f.BH);
+  flash_fwd_kernel<HD, BF16><<<grid, kThreads, FlashSmem<HD>::kBytes, stream>>>(
       q, k, v, o, f.N, f.scale_log2, f.causal ? 1 : 0);
   return cudaGetLastError();
 }
@@ -368,8 +449,7 @@ struct FlashMapCache {
 cudaError_t launch_flash_fwd_tcgen05(const FlashArgs &f, cudaStream_t stream) {
   if (f.dtype != 1 && f.dtype != 2) return cudaErrorInvalidValue;
   if (f.d != 64 && f.d != 128) return cudaErrorInvalidValue;
-  if (f.BH <= 0 || f.N <= 0 || f.BH > 65535 * 32768) return cudaErrorInvalidValue;
-  if ((f.N + BQ - 1) / BQ > 65535) return cudaErrorInvalidValue;
+  if (f.BH <= 0 || f.N <= 0 || f.BH > 65535) return cudaErrorInvalidValue;
   for (const void *p : {f.Q, f.K, f.V, static_cast<const void *>(f.O)})
     if (reinterpret_cast<uintptr_t>(p) & 15u) return cudaErrorInvalidValue;
   const bool bf16 = (f.dtype == 2);

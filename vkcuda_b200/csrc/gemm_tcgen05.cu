@@ -9,6 +9,10 @@
 // Design (one persistent CTA per SM, 192 threads):
 //   warp 0      TMA producer: A tile 128x64 and B tile 64x256 (or 256x64)
 //               per stage, 128-byte swizzled, 4-stage ring (48 KiB/stage).
+//   Work units are 128 x 256 output tiles; when the last partial wave would
+//   fill at most half the SMs, its tiles are split into two 128 x 128 units
+//   each so that the tail costs half a tile time (4096^3: 512 tiles over 148
+//   SMs = 444 full units + 136 half units).
 //   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma
 //               (M=128, N=256, K=16, fp32 accumulator in TMEM), commits each
 //               stage back to the producer and each finished tile to the
@@ -62,7 +66,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmD,
                     const float *__restrict__ Cin, int64_t ldc, int M, int N, int K,
-                    uint32_t idesc, int b_kn) {
+                    uint32_t idesc_full, uint32_t idesc_half, int b_kn, int num_full,
+                    int num_units) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -72,10 +77,21 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles_m = (M + BM - 1) / BM;
   const int tiles_n = (N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n;
   const int kblocks = (K + BK - 1) / BK;
+  // Work unit u: u < num_full is the full 128 x 256 tile u; later units are
+  // the tail tiles split in two 128 x 128 halves (unit -> tile, half).
+  auto unit_tile = [&](int u, int &tm, int &n0, int &width) {
+    int tile = u, half = 0;
+    width = BN;
+    if (u >= num_full) {
+      tile = num_full + (u - num_full) / 2;
+      half = (u - num_full) & 1;
+      width = BN / 2;
+    }
+    tm = tile / tiles_n;
+    n0 = (tile % tiles_n) * BN + half * (BN / 2);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -107,8 +123,11 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
       uint32_t phase = 0;
       uint32_t issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int tm = tile / tiles_n, tn = tile % tiles_n;
+      for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+        int tm, n0, width;
+        unit_tile(u, tm, n0, width);
+        // The whole 256-wide B panel from n0 is loaded for half units too
+        // (the MMA uses its first 128 columns): one transaction size.
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1u)) { ok = false; break; }
           uint8_t *sA = stage_base + stage * kStageBytes;
@@ -118,10 +137,10 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
           if (b_kn) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sB + j * (64 * BK * 2), &tmB, tn * BN + j * 64, kb * BK,
+              tma_load_2d(sB + j * (64 * BK * 2), &tmB, n0 + j * 64, kb * BK,
                           &bars->full[stage]);
           } else {
-            tma_load_2d(sB, &tmB, kb * BK, tn * BN, &bars->full[stage]);
+            tma_load_2d(sB, &tmB, kb * BK, n0, &bars->full[stage]);
           }
           ++issued;
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -142,9 +161,10 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+      for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
+        const uint32_t idesc = (u < num_full) ? idesc_full : idesc_half;
         if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kAccCols;
@@ -173,22 +193,23 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const int etid = threadIdx.x - 64;
-    uint8_t *row_stage[2] = {epi_base + row * 128, epi_base + kEpiBytes + row * 128};
     int local = 0;
     uint32_t chunk_count = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int tm = tile / tiles_n, tn = tile % tiles_n;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+      int tm, n0, width;
+      unit_tile(u, tm, n0, width);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&bars->acc_full[acc], acc_phase)) break;
       tc_fence_after();
-      const int m0 = tm * BM, n0 = tn * BN;
+      const int m0 = tm * BM;
       const int gr = m0 + row;
-      for (int c = 0; c < BN / kEpiCols; ++c) {
+      const int nchunks = width / kEpiCols;
+      for (int c = 0; c < nchunks; ++c) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * kAccCols + c * kEpiCols, v);
         tmem_ld_wait();
-        if (c == BN / kEpiCols - 1) {
+        if (c == nchunks - 1) {
           tc_fence_before();
           mbar_arrive(&bars->acc_empty[acc]);
         }
@@ -203,7 +224,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
         const int buf = chunk_count & 1;
         if (etid == 0) bulk_wait_group_read<1>();
         named_bar_sync(1, kEpiThreads);
-        uint8_t *dst = row_stage[buf];
+        uint8_t *dst = epi_base + buf * kEpiBytes + row * 128;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int phys = j ^ (row & 7);  // 128-byte swizzle of 16-byte chunks
@@ -315,9 +336,17 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
   const int grid = tiles < sms ? tiles : sms;
-  const uint32_t idesc = idesc_f16_f32(BM, BN, g.bf16, false, g.b_kn);
+  // Tail split: when the last partial wave fills at most half the CTAs, its
+  // tiles run as two half-width units each, halving the tail's duration.
+  const int tail = tiles % grid;
+  const bool split = tail > 0 && 2 * tail <= grid;
+  const int num_full = split ? tiles - tail : tiles;
+  const int num_units = split ? num_full + 2 * tail : tiles;
+  const uint32_t idesc_full = idesc_f16_f32(BM, BN, g.bf16, false, g.b_kn);
+  const uint32_t idesc_half = idesc_f16_f32(BM, BN / 2, g.bf16, false, g.b_kn);
   gemm_tcgen05_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      cache.a, cache.b, cache.d, g.Cin, g.ldc, g.M, g.N, g.K, idesc, g.b_kn ? 1 : 0);
+      cache.a, cache.b, cache.d, g.Cin, g.ldc, g.M, g.N, g.K, idesc_full, idesc_half,
+      g.b_kn ? 1 : 0, num_full, num_units);
   return cudaGetLastError();
 }
 

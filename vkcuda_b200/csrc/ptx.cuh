@@ -316,6 +316,18 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n,
          ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// Per-warpgroup register reallocation (all four warps of the warpgroup
+// execute it). The launch-time total (threads x registers at launch) bounds
+// the sum of the warpgroups' shares.
+template <uint32_t R>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
+}
+template <uint32_t R>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R));
+}
+
 // Base-2 exponential on the MUFU unit (PTX ex2.approx, ftz).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
