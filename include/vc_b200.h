@@ -168,6 +168,19 @@ int vc_vadd_f32(const float *a, const float *b, float *c, int64_t n,
  * partials buffer. Replaces the sum of test/reduce.vc scaled to one scalar. */
 int vc_sum_f32(const float *x, int64_t n, double *out, void *stream);
 
+/* No counterpart in the reference. Same result as vc_sum_f32 (same kernel,
+ * grid and summation order) for callers that cannot allocate device memory at
+ * call time (a process whose device budget is fully reserved up front, a
+ * latency-critical loop that must stay out of the driver allocator, a
+ * library callback that must not allocate as a side effect). Allocates
+ * nothing: its block partials live in a fixed 8 KiB array compiled into the
+ * library (1024 partial slots; a device that would need more blocks is
+ * refused with VC_INVALID_VALUE). All calls share that array: calls that
+ * overlap on the GPU race. The first call on a device looks up the array's
+ * address; make it before any stream capture. Uses the calling thread's
+ * current CUDA device. */
+int vc_sum_f32_noalloc(const float *x, int64_t n, double *out, void *stream);
+
 /* Fused: c = a + b and *out = sum(c) in one pass (12 bytes per element). */
 int vc_vadd_sum_f32(const float *a, const float *b, float *c, int64_t n,
                     double *out, void *stream);

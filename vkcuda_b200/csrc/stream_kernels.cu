@@ -16,7 +16,11 @@
 // them in index order. The result is deterministic for a given grid.
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <unordered_map>
 
+#include "../../include/vc_b200.h"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -306,6 +310,93 @@ cudaError_t launch_block_reduce_demo(const float *in, float *out, int n, int blo
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------------
+// Allocation-free sum: vc_sum_f32_noalloc.
+//
+// Some callers cannot allocate device memory at call time: a serving process
+// that reserved its whole device budget at start-up and hands out no more, a
+// latency-critical loop that must not enter the driver allocator (cudaMalloc
+// can synchronise the device and takes a process-wide lock), or a host
+// library calling in from a callback where a first-use allocation would be
+// an unexpected side effect. vc_sum_f32 gets its block partials from a
+// runtime-owned buffer that is cudaMalloc'd on first use per stream; this
+// entry point instead keeps them in a fixed array compiled into the library.
+//
+// The array below exists once per GPU that loads the library and stays
+// resident until the process exits. It holds kNoAllocMaxPartials block
+// partials (8 KiB) plus the ticket counter, which bounds the grid to 1024
+// blocks; the grid is the same one vc_sum_f32 uses (4 blocks per SM at most,
+// 592 on a B200), so both entries add the same partials in the same order.
+// A device that would need more blocks than that is refused with an error.
+// Every call shares the array and it keeps the last call's contents: the
+// ticket is cleared on the stream before each launch (the partial slots are
+// written before they are read), and calls that overlap on the GPU (two
+// streams at once) race on the array.
+constexpr int kNoAllocMaxPartials = 1024;
+
+struct NoAllocSumScratch {
+  double partials[kNoAllocMaxPartials];
+  unsigned int ticket;
+};
+
+static __device__ __align__(256) NoAllocSumScratch g_sum_noalloc_scratch;
+
+// Device address of the array on the current device. In host code the
+// symbol's name is a host-side stand-in, not a device address, so it is
+// looked up once per device (that device current) and cached.
+static cudaError_t noalloc_scratch_address(NoAllocSumScratch **out) {
+  static std::mutex mu;
+  static std::unordered_map<int, NoAllocSumScratch *> by_device;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = by_device.find(dev);
+  if (it == by_device.end()) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_sum_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    it = by_device.emplace(dev, static_cast<NoAllocSumScratch *>(p)).first;
+  }
+  *out = it->second;
+  return cudaSuccess;
+}
+
 }  // namespace vcb
 
 VCB_DEFINE_ERROR_ACCESSOR(stream_kernels_error)
+
+// *out = sum of x[0..n) (device double), like vc_sum_f32, without allocating
+// anything: scratch lives in the library's static device array (see above).
+// The first call on a device looks up that array's address (no allocation);
+// make that first call before any stream capture. Runs on the calling
+// thread's current CUDA device.
+extern "C" int vc_sum_f32_noalloc(const float *x, int64_t n, double *out, void *stream) {
+  using namespace vcb;
+  if (!x || !out || n < 0) return VC_INVALID_VALUE;
+  const bool vec = aligned16(x);
+  const int64_t units = vec ? (n / 4) / kUnroll + 1 : n / kUnroll + 1;
+  const int grid = stream_grid(units);
+  if (grid > kNoAllocMaxPartials) {
+    std::fprintf(stderr,
+                 "vc_sum_f32_noalloc: this device needs %d block partials; the static scratch "
+                 "holds %d\n", grid, kNoAllocMaxPartials);
+    return VC_INVALID_VALUE;
+  }
+  NoAllocSumScratch *scratch = nullptr;
+  cudaError_t e = noalloc_scratch_address(&scratch);
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "vc_sum_f32_noalloc: scratch lookup failed: %s\n", cudaGetErrorString(e));
+    return VC_UNKNOWN;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  e = cudaMemsetAsync(&scratch->ticket, 0, sizeof(unsigned int), s);
+  if (e == cudaSuccess)
+    e = launch_sum_f32(x, nullptr, nullptr, n, out, scratch->partials, &scratch->ticket,
+                       kNoAllocMaxPartials, s);
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "vc_sum_f32_noalloc: %s\n", cudaGetErrorString(e));
+    return VC_UNKNOWN;
+  }
+  return VC_SUCCESS;
+}

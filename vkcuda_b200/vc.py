@@ -137,6 +137,7 @@ SIGNATURES = {
     "vc_kernel_error": (_I, [_I]), "vc_selftest_bounded_wait": (_I, [_U]),
     "vc_vadd_f32": (_I, [_VP, _VP, _VP, _I64, _VP]),
     "vc_sum_f32": (_I, [_VP, _I64, _VP, _VP]),
+    "vc_sum_f32_noalloc": (_I, [_VP, _I64, _VP, _VP]),
     "vc_vadd_sum_f32": (_I, [_VP, _VP, _VP, _I64, _VP, _VP]),
     "vc_block_reduce_f32": (_I, [_VP, _VP, _I, _I, _I, _VP]),
     "vc_gemm": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I64, _I64, _I64, _I64, _I, _I, _VP]),
@@ -418,6 +419,12 @@ def vadd_f32(a, b, c, n: int, stream=None) -> VCError:
 
 def sum_f32(x, n: int, out, stream=None) -> VCError:
     return VCError(library().vc_sum_f32(_addr(x), n, _addr(out), _stream(stream)))
+
+
+def sum_f32_noalloc(x, n: int, out, stream=None) -> VCError:
+    """vc_sum_f32 without allocating: block partials in the library's static
+    device array (see include/vc_b200.h). Overlapping calls race."""
+    return VCError(library().vc_sum_f32_noalloc(_addr(x), n, _addr(out), _stream(stream)))
 
 
 def vadd_sum_f32(a, b, c, n: int, out, stream=None) -> VCError:
