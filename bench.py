@@ -447,7 +447,9 @@ def cpu_gemm_baseline(target_s=8.0):
     rng = np.random.default_rng(7)
     a = (rng.random((N, N), dtype=np.float32) * 2 - 1).astype(np.float16).astype(np.float32)
     b = (rng.random((N, N), dtype=np.float32) * 2 - 1).astype(np.float16).astype(np.float32)
-    threads = oracle.max_threads()
+    # All host cores this process may run on (torchrun sets OMP_NUM_THREADS=1
+    # for its workers; the baseline overrides it explicitly).
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     rows = max(2, threads)
     t0 = time.perf_counter()
     oracle.gemm(a, b, N, N, N, N, N, True, rows=(0, rows), threads=threads)
