@@ -297,11 +297,17 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             if (key >= N || (causal && key > qi)) s[c][t] = __float_as_uint(-INFINITY);
           }
       }
-      float mx = -INFINITY;
+      // Row max with 8 independent partial maxima: a 128-long dependent
+      // chain would dominate the tile's latency.
+      float mxp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BKV / 32; ++c)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) mx = fmaxf(mx, __uint_as_float(s[c][t]));
+        for (int t = 0; t < 32; ++t) mxp[t & 7] = fmaxf(mxp[t & 7], __uint_as_float(s[c][t]));
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       const float m_cand = fmaxf(m_run, mx * scale_log2);
       const bool grow = m_cand > m_run + kRescaleThreshold;  // true on the first tile
       // Warp-uniform decision (TMEM loads and stores are warp-collective).
@@ -318,7 +324,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       // P = exp2(scale_log2 * s - m) -> 16-bit pairs over S columns; one in
       // four exponentials runs on the FMA pipe (exp2_poly) to offload MUFU.
       // The row sum adds the rounded values.
-      float lsum = 0.0f;
+      float lsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
       for (int c = 0; c < BKV / 32; ++c) {
         uint32_t p[16];
@@ -330,11 +336,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
           const float p0 = ex2_approx(x0);
           const float p1 = (t & 1) ? exp2_poly(x1) : ex2_approx(x1);
           p[t] = pack2<BF16>(p0, p1);
-          lsum += sum2<BF16>(p[t]);
+          lsp[t & 7] += sum2<BF16>(p[t]);
         }
         tmem_st16(s_col + c * 16, p);
       }
-      l_run += lsum;
+      l_run += ((lsp[0] + lsp[1]) + (lsp[2] + lsp[3])) + ((lsp[4] + lsp[5]) + (lsp[6] + lsp[7]));
       if (rescale && j > 0) {
         // S_w(j) complete implies PV_w(j-1) complete: O_w is stable. Done
         // after P so that S is no longer live in registers.

@@ -6,7 +6,10 @@
 // examples/matmul_coopmat_bench.vc:60-110 (16x16 tiles of 2x2 8x8x16 MMAs,
 // accumulator streamed through global C every K step).
 //
-// Design (one persistent CTA per SM, 192 threads):
+// Two kernels: gemm_tcgen05_pair_kernel (CTA pairs, cta_group::2, used when
+// M > 128; described at its definition) and the single-CTA kernel below.
+//
+// Single-CTA design (one persistent CTA per SM, 192 threads):
 //   warp 0      TMA producer: A tile 128x64 and B tile 64x256 (or 256x64)
 //               per stage, 128-byte swizzled, 4-stage ring (48 KiB/stage).
 //   Work units are 128 x 256 output tiles; when the last partial wave would
@@ -249,6 +252,230 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// ------------------------------------------------------------ CTA-pair kernel
+// Same contract, for problems with at least two 128-row blocks: clusters of
+// two CTAs drive one cta_group::2 MMA of M = 256 (128 rows per CTA), N = 256.
+// Each CTA loads its own 128 rows of A and its own 128-column half of the B
+// panel (16 + 16 KiB per 64-deep stage), so a CTA reads 32 KiB from L2 per
+// stage instead of 48 KiB for the same 128 x 256 outputs. CTA 0 issues the
+// MMAs; both CTAs' TMA copies count on CTA 0's full barriers; CTA 0's commits
+// release the empty barriers and accumulator-full barriers of both CTAs; both
+// epilogues release CTA 0's accumulator-empty barriers. Each CTA's TMEM holds
+// its 128 accumulator rows (2 x 256 columns, double-buffered). Work units are
+// 256 x 256 pair tiles; a tail wave that fills at most half the clusters is
+// split into 256 x 128 halves.
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairABytes = 128 * BK * 2;  // this CTA's A rows
+constexpr uint32_t kPairBBytes = 128 * BK * 2;  // this CTA's half of the B panel
+constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;
+
+struct __align__(8) PairBarriers {
+  uint64_t full[kPairStages];   // used in CTA 0
+  uint64_t empty[kPairStages];  // both CTAs
+  uint64_t acc_full[2];         // both CTAs
+  uint64_t acc_empty[2];        // used in CTA 0 (both epilogues arrive)
+  uint32_t tmem_base;
+};
+
+constexpr size_t kPairSmemBytes =
+    1024 + kPairStages * kPairStageBytes + 2 * kEpiBytes + sizeof(PairBarriers);
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmD,
+                         const float *__restrict__ Cin, int64_t ldc, int M, int N, int K,
+                         uint32_t idesc_full, uint32_t idesc_half, int b_kn, int num_full,
+                         int num_units) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *stage_base = smem;
+  uint8_t *epi_base = smem + kPairStages * kPairStageBytes;
+  PairBarriers *bars = reinterpret_cast<PairBarriers *>(epi_base + 2 * kEpiBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int kblocks = (K + BK - 1) / BK;
+  auto unit_tile = [&](int u, int &tm, int &n0, int &width) {
+    int tile = u, half = 0;
+    width = BN;
+    if (u >= num_full) {
+      tile = num_full + (u - num_full) / 2;
+      half = (u - num_full) & 1;
+      width = BN / 2;
+    }
+    tm = tile / tiles_n;
+    n0 = (tile % tiles_n) * BN + half * (BN / 2);
+  };
+  // Barrier addresses in the cluster window.
+  auto lead = [&](uint64_t *b) { return mapa_shared(smem_u32(b), 0); };
+  auto peer = [&](uint64_t *b) { return mapa_shared(smem_u32(b), 1); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 2 * kEpiThreads);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmD);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int u = cluster; ok && u < num_units; u += num_clusters) {
+        int tm, n0, width;
+        unit_tile(u, tm, n0, width);
+        const int a_row = tm * 2 * BM + rank * BM;
+        const int b_col = n0 + rank * (width / 2);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bars->empty[stage], phase ^ 1u)) { ok = false; break; }
+          uint8_t *sA = stage_base + stage * kPairStageBytes;
+          uint8_t *sB = sA + kPairABytes;
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * kPairStageBytes);
+          const uint32_t fb = lead(&bars->full[stage]);
+          tma_load_2d_pair(sA, &tmA, kb * BK, a_row, fb);
+          if (b_kn) {
+            tma_load_2d_pair(sB, &tmB, b_col, kb * BK, fb);
+            tma_load_2d_pair(sB + 64 * BK * 2, &tmB, b_col + 64, kb * BK, fb);
+          } else {
+            tma_load_2d_pair(sB, &tmB, kb * BK, b_col, fb);
+          }
+          ++issued;
+          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain (CTA 0 sees both CTAs' bytes on its full barriers).
+      if (rank == 0) {
+        const uint32_t last = issued < (uint32_t)kPairStages ? issued : (uint32_t)kPairStages;
+        for (uint32_t i = 0; i < last; ++i) {
+          const uint32_t idx = issued - 1 - i;
+          mbar_wait(&bars->full[idx % kPairStages], (idx / kPairStages) & 1u, 1000000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (CTA 0)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int u = cluster; ok && u < num_units; u += num_clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        const uint32_t idesc = (u < num_full) ? idesc_full : idesc_half;
+        if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kAccCols;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bars->full[stage], phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(stage_base + stage * kPairStageBytes);
+          const uint32_t b_addr = a_addr + kPairABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc =
+                b_kn ? smem_desc_sw128(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
+                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(lead(&bars->empty[stage]));
+          mma_commit_pair(peer(&bars->empty[stage]));
+          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit_pair(lead(&bars->acc_full[acc]));
+        mma_commit_pair(peer(&bars->acc_full[acc]));
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): warps 2..5, thread = row
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int etid = threadIdx.x - 64;
+    const uint32_t acc_empty_lead[2] = {lead(&bars->acc_empty[0]), lead(&bars->acc_empty[1])};
+    int local = 0;
+    uint32_t chunk_count = 0;
+    for (int u = cluster; u < num_units; u += num_clusters, ++local) {
+      int tm, n0, width;
+      unit_tile(u, tm, n0, width);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&bars->acc_full[acc], acc_phase)) break;
+      tc_fence_after();
+      const int m0 = tm * 2 * BM + rank * BM;
+      const int gr = m0 + row;
+      const int nchunks = width / kEpiCols;
+      for (int c = 0; c < nchunks; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * kAccCols + c * kEpiCols, v);
+        tmem_ld_wait();
+        if (c == nchunks - 1) {
+          tc_fence_before();
+          if (rank == 0) mbar_arrive(&bars->acc_empty[acc]);
+          else mbar_arrive_cluster(acc_empty_lead[acc]);
+        }
+        const int cn0 = n0 + c * kEpiCols;
+        if (cn0 >= N) continue;
+        if (Cin != nullptr && gr < M) {
+          const float *crow = Cin + (int64_t)gr * ldc;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (cn0 + j < N) v[j] = __float_as_uint(__uint_as_float(v[j]) + crow[cn0 + j]);
+        }
+        const int buf = chunk_count & 1;
+        if (etid == 0) bulk_wait_group_read<1>();
+        named_bar_sync(1, kEpiThreads);
+        uint8_t *dst = epi_base + buf * kEpiBytes + row * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int phys = j ^ (row & 7);
+          *reinterpret_cast<uint4 *>(dst + phys * 16) =
+              make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, kEpiThreads);
+        if (etid == 0) {
+          tma_store_2d(&tmD, epi_base + buf * kEpiBytes, cn0, m0);
+          bulk_commit_group();
+        }
+        ++chunk_count;
+      }
+    }
+    if (etid == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before();
+  cluster_sync();  // both CTAs done with TMEM and with each other's barriers
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
+}
+
 // ------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t,
                                   void *, const cuuint64_t *, const cuuint64_t *,
@@ -275,7 +502,7 @@ bool make_map_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes,
 struct MapCache {
   GemmArgs key{};
   int device = -1;
-  CUtensorMap a, b, d;
+  CUtensorMap a, b, b_pair, d;
   bool valid = false;
 };
 
@@ -286,6 +513,26 @@ bool same_key(const GemmArgs &x, const GemmArgs &y) {
 }
 
 bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Clusters of two that can be resident at once (SM pairs within GPCs); the
+// persistent grid must not exceed it or late clusters would run a second wave.
+int pair_clusters_resident(int dev, int sms) {
+  static int cached[64] = {0};
+  if (dev < 0 || dev >= 64) return sms / 2;
+  if (cached[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms & ~1, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tcgen05_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sms / 2;
+    }
+    cached[dev] = n < sms / 2 ? n : sms / 2;
+  }
+  return cached[dev];
+}
 
 }  // namespace
 
@@ -305,10 +552,13 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
     const CUtensorMapDataType t16 =
         g.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     bool ok = make_map_2d(&cache.a, t16, 2, g.A, g.K, g.M, g.lda, BK, BM);
-    if (g.b_kn)
+    if (g.b_kn) {
       ok = ok && make_map_2d(&cache.b, t16, 2, g.B, g.N, g.K, g.ldb, 64, BK);
-    else
+      cache.b_pair = cache.b;
+    } else {
       ok = ok && make_map_2d(&cache.b, t16, 2, g.B, g.K, g.N, g.ldb, BK, BN);
+      ok = ok && make_map_2d(&cache.b_pair, t16, 2, g.B, g.K, g.N, g.ldb, BK, BN / 2);
+    }
     ok = ok && make_map_2d(&cache.d, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.D, g.N, g.M,
                            g.ldd, kEpiCols, BM);
     if (!ok) {
@@ -328,12 +578,32 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
       cudaError_t e = cudaFuncSetAttribute(gemm_tcgen05_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)kSmemBytes);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_tcgen05_pair_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kPairSmemBytes);
       if (e != cudaSuccess) return e;
       configured_device_mask |= (1 << dev);
     }
   }
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (g.M > BM && sms >= 2) {
+    // CTA-pair kernel: 256 x 256 pair tiles over sms / 2 clusters.
+    const int pair_tiles = ((g.M + 2 * BM - 1) / (2 * BM)) * ((g.N + BN - 1) / BN);
+    const int resident = pair_clusters_resident(dev, sms);
+    const int clusters = pair_tiles < resident ? pair_tiles : resident;
+    const int tail = pair_tiles % clusters;
+    const bool split = tail > 0 && 2 * tail <= clusters;
+    const int num_full = split ? pair_tiles - tail : pair_tiles;
+    const int num_units = split ? num_full + 2 * tail : pair_tiles;
+    const uint32_t idesc_full = idesc_f16_f32(2 * BM, BN, g.bf16, false, g.b_kn);
+    const uint32_t idesc_half = idesc_f16_f32(2 * BM, BN / 2, g.bf16, false, g.b_kn);
+    gemm_tcgen05_pair_kernel<<<2 * clusters, kThreads, kPairSmemBytes, stream>>>(
+        cache.a, cache.b_pair, cache.d, g.Cin, g.ldc, g.M, g.N, g.K, idesc_full, idesc_half,
+        g.b_kn ? 1 : 0, num_full, num_units);
+    return cudaGetLastError();
+  }
   const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
   const int grid = tiles < sms ? tiles : sms;
   // Tail split: when the last partial wave fills at most half the CTAs, its
