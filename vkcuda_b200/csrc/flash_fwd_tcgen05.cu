@@ -28,10 +28,11 @@
 //               row max, conditional rescale of O (only when the max grows
 //               by more than 2^8; p <= 256 otherwise and the final 1/l makes
 //               it exact), P = exp2(scale_log2 * s - m) rounded to 16 bits,
-//               row sum of the rounded P (numerator and denominator use the
-//               same weights). One exponential in four runs as a polynomial
-//               on the FMA pipe, which relieves the MUFU unit (16 ex2 per
-//               clock per SM against 8192 MMA FLOP per clock). At the end O / l is staged over the Q tile and
+//               row sum (of the rounded P for bf16, so numerator and
+//               denominator use the same weights). The softmax is bound by
+//               instruction issue, not by the MUFU exponential unit: moving a
+//               share of the exponentials to an FMA-pipe polynomial measured
+//               slower (1/16: -2 %, 1/4: -10 %, 1/2: -25 %), so all use MUFU. At the end O / l is staged over the Q tile and
 //               stored with TMA.
 // Causal: Q0 of query block b uses key tiles 0..2b, Q1 0..2b+1; blocks are
 // scheduled heaviest first. Keys >= N and keys above the diagonal are masked.
@@ -60,6 +61,7 @@ constexpr int kWgThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kBoxBytes = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
 
 struct __align__(8) FlashBarriers {
   uint64_t q_full;
@@ -102,23 +104,6 @@ __device__ __forceinline__ float sum2(uint32_t w) {
     const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
     return f.x + f.y;
   }
-}
-
-// 2^x on the FMA pipe: x = i + f with i = round(x) (the 1.5 * 2^23 shifter
-// leaves round(x) in the low mantissa bits), f in [-0.5, 0.5]; 2^f by a
-// degree-3 polynomial fitted here to 2^f on that interval (iterated weighted
-// least squares on Chebyshev nodes, max relative error 7.5e-5, below the
-// 16-bit rounding of P); 2^i by adding i to the exponent field. Inputs below
-// -126 (including -inf for masked scores) return exactly 0, like the ftz
-// MUFU exponential.
-__device__ __forceinline__ float exp2_poly(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float shifter = 12582912.0f;
-  const float t = xc + shifter;
-  const float f = xc - (t - shifter);
-  const float p = fmaf(fmaf(fmaf(0.055171654f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
-  const int i = __float_as_int(t) - __float_as_int(shifter);
-  return x < -126.0f ? 0.0f : __int_as_float(__float_as_int(p) + (i << 23));
 }
 
 template <int HD, bool BF16>
@@ -208,14 +193,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       // ------------------------------------------------ MMA issuer
       const uint32_t idesc_s = idesc_f16_f32(BQ, BKV, BF16, false, false);
       const uint32_t idesc_o = idesc_f16_f32(BQ, HD, BF16, false, true);
-      const uint32_t q_addr[2] = {smem_u32(smem + L::kQ0), smem_u32(smem + L::kQ1)};
+      const uint32_t q0_addr = smem_u32(smem + L::kQ0), q1_addr = smem_u32(smem + L::kQ1);
       const uint32_t ring = smem_u32(smem + L::kRing);
       auto issue_s = [&](int w, uint32_t k_idx) {
         const uint32_t kaddr = ring + (k_idx % kStages) * L::kTile;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
           const uint32_t off = (ks / 4) * kBoxBytes + (ks % 4) * 32;
-          mma_f16_ss(tmem + w * 128, smem_desc_sw128(q_addr[w] + off, 16, 1024),
+          mma_f16_ss(tmem + w * 128, smem_desc_sw128((w ? q1_addr : q0_addr) + off, 16, 1024),
                      smem_desc_sw128(kaddr + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
         }
         mma_commit(&bars->s_full[w]);
@@ -289,25 +274,23 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       for (int c = 0; c < BKV / 32; ++c) tmem_ld32(s_col + c * 32, s[c]);
       tmem_ld_wait();
       if (need_mask) {
+        // Keys key0 + t with t >= valid are masked (past N, or above the
+        // diagonal for causal): one compare per element.
+        int valid = N - key0;
+        if (causal) valid = min(valid, qi - key0 + 1);
 #pragma unroll
         for (int c = 0; c < BKV / 32; ++c)
 #pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const int key = key0 + c * 32 + t;
-            if (key >= N || (causal && key > qi)) s[c][t] = __float_as_uint(-INFINITY);
-          }
+          for (int t = 0; t < 32; ++t)
+            if (c * 32 + t >= valid) s[c][t] = __float_as_uint(-INFINITY);
       }
-      // Row max with 8 independent partial maxima: a 128-long dependent
-      // chain would dominate the tile's latency.
-      float mxp[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
+      // Row max with 4 independent partial maxima (shorter dependent chain).
+      float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < BKV / 32; ++c)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) mxp[t & 7] = fmaxf(mxp[t & 7], __uint_as_float(s[c][t]));
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        for (int t = 0; t < 32; ++t) mxp[t & 3] = fmaxf(mxp[t & 3], __uint_as_float(s[c][t]));
+      const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
       const float m_cand = fmaxf(m_run, mx * scale_log2);
       const bool grow = m_cand > m_run + kRescaleThreshold;  // true on the first tile
       // Warp-uniform decision (TMEM loads and stores are warp-collective).
@@ -321,10 +304,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         m_run = m_cand;
       }
       const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-      // P = exp2(scale_log2 * s - m) -> 16-bit pairs over S columns; one in
-      // four exponentials runs on the FMA pipe (exp2_poly) to offload MUFU.
-      // The row sum adds the rounded values.
-      float lsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+      // P = exp2(scale_log2 * s - m) -> 16-bit pairs over S columns.
+      float lsp[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
       for (int c = 0; c < BKV / 32; ++c) {
         uint32_t p[16];
@@ -332,15 +313,19 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         for (int t = 0; t < 16; ++t) {
           const float x0 = fmaf(__uint_as_float(s[c][2 * t]), scale_log2, -m_use);
           const float x1 = fmaf(__uint_as_float(s[c][2 * t + 1]), scale_log2, -m_use);
-          // Masked scores are -inf: both exponentials return exactly 0.
+          // Masked scores are -inf: the exponential returns exactly 0.
           const float p0 = ex2_approx(x0);
-          const float p1 = (t & 1) ? exp2_poly(x1) : ex2_approx(x1);
+          const float p1 = ex2_approx(x1);
           p[t] = pack2<BF16>(p0, p1);
-          lsp[t & 7] += sum2<BF16>(p[t]);
+          // bf16 P (8-bit mantissa): the row sum adds the rounded values so
+          // numerator and denominator use the same weights; fp16 P (11 bits)
+          // is close enough that the unrounded sum keeps O within its bar
+          // and saves the unpacking.
+          lsp[t & 3] += BF16 ? sum2<BF16>(p[t]) : (p0 + p1);
         }
         tmem_st16(s_col + c * 16, p);
       }
-      l_run += ((lsp[0] + lsp[1]) + (lsp[2] + lsp[3])) + ((lsp[4] + lsp[5]) + (lsp[6] + lsp[7]));
+      l_run += (lsp[0] + lsp[1]) + (lsp[2] + lsp[3]);
       if (rescale && j > 0) {
         // S_w(j) complete implies PV_w(j-1) complete: O_w is stable. Done
         // after P so that S is no longer live in registers.

@@ -418,7 +418,8 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const int etid = threadIdx.x - 64;
-    const uint32_t acc_empty_lead[2] = {lead(&bars->acc_empty[0]), lead(&bars->acc_empty[1])};
+    const uint32_t acc_empty_lead0 = lead(&bars->acc_empty[0]);
+    const uint32_t acc_empty_lead1 = lead(&bars->acc_empty[1]);
     int local = 0;
     uint32_t chunk_count = 0;
     for (int u = cluster; u < num_units; u += num_clusters, ++local) {
@@ -438,7 +439,7 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         if (c == nchunks - 1) {
           tc_fence_before();
           if (rank == 0) mbar_arrive(&bars->acc_empty[acc]);
-          else mbar_arrive_cluster(acc_empty_lead[acc]);
+          else mbar_arrive_cluster(acc ? acc_empty_lead1 : acc_empty_lead0);
         }
         const int cn0 = n0 + c * kEpiCols;
         if (cn0 >= N) continue;
