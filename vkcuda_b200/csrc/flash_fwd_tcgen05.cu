@@ -95,17 +95,6 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
-// Sum of the two 16-bit values of a packed pair, in fp32.
-template <bool BF16>
-__device__ __forceinline__ float sum2(uint32_t w) {
-  if constexpr (BF16) {
-    return __uint_as_float(w << 16) + __uint_as_float(w & 0xffff0000u);
-  } else {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
-    return f.x + f.y;
-  }
-}
-
 template <int HD, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -284,13 +273,16 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
           for (int t = 0; t < 32; ++t)
             if (c * 32 + t >= valid) s[c][t] = __float_as_uint(-INFINITY);
       }
-      // Row max with 4 independent partial maxima (shorter dependent chain).
+      // Row max: three-input max (two new values per instruction) into 4
+      // independent partial maxima (short dependent chains).
       float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < BKV / 32; ++c)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) mxp[t & 3] = fmaxf(mxp[t & 3], __uint_as_float(s[c][t]));
-      const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+        for (int t = 0; t < 32; t += 2)
+          mxp[(t >> 1) & 3] = fmax3(mxp[(t >> 1) & 3], __uint_as_float(s[c][t]),
+                                    __uint_as_float(s[c][t + 1]));
+      const float mx = fmax3(fmaxf(mxp[0], mxp[1]), mxp[2], mxp[3]);
       const float m_cand = fmaxf(m_run, mx * scale_log2);
       const bool grow = m_cand > m_run + kRescaleThreshold;  // true on the first tile
       // Warp-uniform decision (TMEM loads and stores are warp-collective).
@@ -305,14 +297,17 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       }
       const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
       // P = exp2(scale_log2 * s - m) -> 16-bit pairs over S columns.
-      float lsp[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
+      // Two packed (f32x2) partial-sum pairs.
+      float lsp[4] = {0.f, 0.f, 0.f, 0.f};
+      const float neg_m = -m_use;
 #pragma unroll
       for (int c = 0; c < BKV / 32; ++c) {
         uint32_t p[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          const float x0 = fmaf(__uint_as_float(s[c][2 * t]), scale_log2, -m_use);
-          const float x1 = fmaf(__uint_as_float(s[c][2 * t + 1]), scale_log2, -m_use);
+          float x0, x1;
+          fma2(x0, x1, __uint_as_float(s[c][2 * t]), __uint_as_float(s[c][2 * t + 1]), scale_log2,
+               scale_log2, neg_m, neg_m);
           // Masked scores are -inf: the exponential returns exactly 0.
           const float p0 = ex2_approx(x0);
           const float p1 = ex2_approx(x1);
@@ -321,7 +316,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
           // numerator and denominator use the same weights; fp16 P (11 bits)
           // is close enough that the unrounded sum keeps O within its bar
           // and saves the unpacking.
-          lsp[t & 3] += BF16 ? sum2<BF16>(p[t]) : (p0 + p1);
+          const int a = 2 * (t & 1);
+          if constexpr (BF16)
+            add2(lsp[a], lsp[a + 1], lsp[a], lsp[a + 1], __uint_as_float(p[t] << 16),
+                 __uint_as_float(p[t] & 0xffff0000u));
+          else
+            add2(lsp[a], lsp[a + 1], lsp[a], lsp[a + 1], p0, p1);
         }
         tmem_st16(s_col + c * 16, p);
       }
