@@ -22,8 +22,9 @@
 //               epilogue. Two accumulators (2 x 256 columns) alternate, so
 //               the MMAs of tile i+1 overlap the epilogue of tile i.
 //   warps 2..5  epilogue: tcgen05.ld 32 columns per thread-row, optional
-//               Cin addend, swizzled staging in shared memory (2 x 16 KiB),
-//               TMA store of 128x32 fp32 boxes.
+//               Cin addend; each warp stages its own 32 x 32 fp32 box in
+//               shared memory (2 x 4 KiB per warp, 128-byte swizzle) and
+//               TMA-stores it, with no barrier between the warps.
 // Ragged M, N and K are handled by TMA: loads zero-fill outside the matrix
 // and stores clip, so any shape whose row strides meet TMA's 16-byte rule
 // runs here. Roofline: 2*M*N*K FLOP against the dense fp16/bf16 tensor peak.
@@ -60,6 +61,31 @@ struct __align__(8) GemmBarriers {
   uint64_t acc_empty[2];
   uint32_t tmem_base;
 };
+
+// Epilogue store of one 32 x 32 fp32 box: this warp's 32 accumulator rows
+// (one per lane) x 32 columns. Each warp owns two 4 KiB staging buffers and
+// its own bulk-store groups, so the four epilogue warps never wait for each
+// other. The box is written with the 128-byte swizzle the D tensor map uses.
+__device__ __forceinline__ void epilogue_store_box(const CUtensorMap *tmD, uint8_t *warp_stage,
+                                                   uint32_t (&v)[32], int lane, uint32_t &count,
+                                                   int x, int y) {
+  const int buf = count & 1;
+  if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` has read it
+  __syncwarp();
+  uint8_t *box = warp_stage + buf * 4096;
+  uint8_t *dst = box + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<uint4 *>(dst + ((j ^ (lane & 7)) * 16)) =
+        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmD, box, x, y);
+    bulk_commit_group();
+  }
+  ++count;
+}
 
 constexpr size_t kSmemBytes =
     1024 /* alignment slack */ + kStages * kStageBytes + 2 * kEpiBytes + sizeof(GemmBarriers);
@@ -195,7 +221,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
     // ---------------- epilogue: warps 2..5, thread = accumulator row
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
-    const int etid = threadIdx.x - 64;
+    uint8_t *warp_stage = epi_base + quad * 8192;
     int local = 0;
     uint32_t chunk_count = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
@@ -224,26 +250,10 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
           for (int j = 0; j < 32; ++j)
             if (cn0 + j < N) v[j] = __float_as_uint(__uint_as_float(v[j]) + crow[cn0 + j]);
         }
-        const int buf = chunk_count & 1;
-        if (etid == 0) bulk_wait_group_read<1>();
-        named_bar_sync(1, kEpiThreads);
-        uint8_t *dst = epi_base + buf * kEpiBytes + row * 128;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int phys = j ^ (row & 7);  // 128-byte swizzle of 16-byte chunks
-          *reinterpret_cast<uint4 *>(dst + phys * 16) =
-              make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        }
-        fence_proxy_async_smem();
-        named_bar_sync(1, kEpiThreads);
-        if (etid == 0) {
-          tma_store_2d(&tmD, epi_base + buf * kEpiBytes, cn0, m0);
-          bulk_commit_group();
-        }
-        ++chunk_count;
+        epilogue_store_box(&tmD, warp_stage, v, lane, chunk_count, cn0, m0 + quad * 32);
       }
     }
-    if (etid == 0) bulk_wait_group<0>();
+    if (lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -417,7 +427,7 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     // ---------------- epilogue (both CTAs): warps 2..5, thread = row
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const int etid = threadIdx.x - 64;
+    uint8_t *warp_stage = epi_base + quad * 8192;
     const uint32_t acc_empty_lead0 = lead(&bars->acc_empty[0]);
     const uint32_t acc_empty_lead1 = lead(&bars->acc_empty[1]);
     int local = 0;
@@ -449,26 +459,10 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
           for (int j = 0; j < 32; ++j)
             if (cn0 + j < N) v[j] = __float_as_uint(__uint_as_float(v[j]) + crow[cn0 + j]);
         }
-        const int buf = chunk_count & 1;
-        if (etid == 0) bulk_wait_group_read<1>();
-        named_bar_sync(1, kEpiThreads);
-        uint8_t *dst = epi_base + buf * kEpiBytes + row * 128;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int phys = j ^ (row & 7);
-          *reinterpret_cast<uint4 *>(dst + phys * 16) =
-              make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        }
-        fence_proxy_async_smem();
-        named_bar_sync(1, kEpiThreads);
-        if (etid == 0) {
-          tma_store_2d(&tmD, epi_base + buf * kEpiBytes, cn0, m0);
-          bulk_commit_group();
-        }
-        ++chunk_count;
+        epilogue_store_box(&tmD, warp_stage, v, lane, chunk_count, cn0, m0 + quad * 32);
       }
     }
-    if (etid == 0) bulk_wait_group<0>();
+    if (lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -561,7 +555,7 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
       ok = ok && make_map_2d(&cache.b_pair, t16, 2, g.B, g.K, g.N, g.ldb, BK, BN / 2);
     }
     ok = ok && make_map_2d(&cache.d, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.D, g.N, g.M,
-                           g.ldd, kEpiCols, BM);
+                           g.ldd, kEpiCols, 32);
     if (!ok) {
       cache.valid = false;
       return cudaErrorNotSupported;
