@@ -30,9 +30,11 @@
 //               it exact), P = exp2(scale_log2 * s - m) rounded to 16 bits,
 //               row sum (of the rounded P for bf16, so numerator and
 //               denominator use the same weights). The softmax is bound by
-//               instruction issue, not by the MUFU exponential unit: moving a
-//               share of the exponentials to an FMA-pipe polynomial measured
-//               slower (1/16: -2 %, 1/4: -10 %, 1/2: -25 %), so all use MUFU. At the end O / l is staged over the Q tile and
+//               instruction issue and latency, not by the MUFU exponential
+//               unit: moving a share of the exponentials to an FMA-pipe
+//               polynomial measured slower or equal (scalar: 1/16 -2 %,
+//               1/4 -10 %, 1/2 -25 %; packed f32x2: 1/8 +-1 %, 1/4 -4 %),
+//               so all use MUFU. At the end O / l is staged over the Q tile and
 //               stored with TMA.
 // Causal: Q0 of query block b uses key tiles 0..2b, Q1 0..2b+1; blocks are
 // scheduled heaviest first. Keys >= N and keys above the diagonal are masked.
@@ -61,6 +63,7 @@ constexpr int kWgThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kBoxBytes = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
 
 
 struct __align__(8) FlashBarriers {
