@@ -144,6 +144,10 @@ int vc_launch_kernel_2d_s(void *kernel, unsigned gridX, unsigned gridY,
                           unsigned blockX, unsigned blockY,
                           const vc_kernel_arg *args, int argCount,
                           void *stream);                                /* :717 */
+int vc_launch_kernel_indirect_s(void *kernel, void *indirectArgs, size_t offset,
+                                unsigned blockX, unsigned blockY, unsigned blockZ,
+                                const vc_kernel_arg *args, int argCount,
+                                void *stream);                          /* :730 */
 const char *vc_error_string(int err);                /* vcErrorString  :743 */
 
 /* Extensions of the runtime API (no reference counterpart). */

@@ -124,3 +124,16 @@ def test_fault_injection_malloc_and_launch():
     assert a == c and a in (0, 5)      # real result: Success on a GPU, InitializationError on CPU
     assert l1 == 8                     # Unknown injected on launch 1
     assert l2 != 8
+
+
+def test_python_mirror_covers_the_api(vc):
+    """Every vc:: function of the header has a Python mirror of the same name,
+    except the storage-image and printf-layer calls (graphics API, out of
+    scope on this runtime)."""
+    text = open(os.path.join(ROOT, "include", "vc", "Runtime", "VCRuntime.h")).read()
+    names = sorted(set(re.findall(r"^(?:VCError|const char \*)\s*(vc\w+)\(", text, re.M)))
+    out_of_scope = {"vcCreateImage1D", "vcCreateImage2D", "vcCreateImage2DArray",
+                    "vcCreateImage3D", "vcDestroyImage", "vcMemcpyToImage",
+                    "vcMemcpyFromImage", "vcEnableKernelPrintf"}
+    missing = [n for n in names if n not in out_of_scope and not hasattr(vc, n)]
+    assert not missing, missing

@@ -67,7 +67,9 @@ def test_flash_attn_legacy_constants(gpu, dev, orc):
 
 
 @pytest.mark.parametrize("BH,N,d,causal", [(1, 256, 64, False), (2, 100, 16, True),
-                                           (3, 333, 128, False), (2, 64, 32, True)])
+                                           (3, 333, 128, False), (2, 64, 32, True),
+                                           (2, 97, 24, True), (1, 130, 48, False),
+                                           (1, 64, 100, True), (3, 40, 8, False)])
 def test_flash_f32_vs_oracle(gpu, dev, orc, BH, N, d, causal):
     rng = np.random.default_rng(BH * N + d)
     Q, K, V = (rng.standard_normal(BH * N * d).astype(np.float32) for _ in range(3))

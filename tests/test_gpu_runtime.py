@@ -6,6 +6,7 @@ peer copies, and the bounded-wait failure path."""
 from __future__ import annotations
 
 import ctypes
+import subprocess
 import threading
 
 import numpy as np
@@ -154,3 +155,102 @@ def test_bounded_wait_reports_timeout_and_context_survives(gpu, dev, orc):
     assert gpu.vcDeviceSynchronize() == 0
     assert (dc.to_host(np.float32, 1000) == 2.0).all()
     assert gpu.kernel_error(True) == 0
+
+
+def test_indirect_launch_reads_workgroups_from_device(gpu, dev, orc):
+    """vcLaunchKernelIndirect: the workgroup counts {x, y, z} come from a device
+    buffer at a byte offset (reference VCRuntime.h:722-740)."""
+    n = 4096
+    rng = np.random.default_rng(8)
+    a = rng.random(n, dtype=np.float32)
+    b = rng.random(n, dtype=np.float32)
+    da, db, dc = dev.put(a), dev.put(b), dev.alloc(4 * n)
+    # {x, y, z} = {n/256 - 4, 1, 1} at byte offset 8: the last 4 workgroups
+    # (1024 elements) are not launched and keep their zeros.
+    ind = dev.put(np.array([7, 7, n // 256 - 4, 1, 1], np.uint32))
+    assert gpu.vcMemset(dc.ptr, 0, 4 * n) == 0
+    err, k = gpu.vcLoadKernel(None, "vadd")
+    args = [gpu.ptr(da.ptr), gpu.ptr(db.ptr), gpu.ptr(dc.ptr), gpu.i32(n)]
+    assert gpu.vcLaunchKernelIndirect(k, ind.ptr, 8, (256, 1, 1), args) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    got = dc.to_host(np.float32, n)
+    assert np.array_equal(got[:n - 1024], orc.vadd(a, b)[:n - 1024])
+    assert not got[n - 1024:].any()
+    # Counts past the end of the buffer are refused.
+    assert gpu.vcLaunchKernelIndirect(k, ind.ptr, 16, (256, 1, 1), args) == gpu.VCError.InvalidValue
+    gpu.vcReleaseKernel(k)
+
+
+def _child(code: str, env: dict) -> subprocess.CompletedProcess:
+    import os
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    return subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                          env=dict(os.environ, **env), cwd=root, timeout=300)
+
+
+def test_profile_table_at_shutdown(gpu):
+    """VC_PROFILE=1: per-op GPU spans summarised at vcShutdown (reference
+    VCRuntime.cpp:1976-2078)."""
+    r = _child("from vkcuda_b200 import vc\n"
+               "import numpy as np\n"
+               "assert vc.vcInit() == 0\n"
+               "e, d = vc.vcMalloc(1 << 20)\n"
+               "x = np.ones(1 << 18, np.float32)\n"
+               "assert vc.vcMemcpy(d, x, x.nbytes, vc.VCMemcpyKind.HostToDevice) == 0\n"
+               "e, k = vc.vcLoadKernel(None, 'vadd')\n"
+               "assert vc.vcLaunchKernel(k, 1 << 18, 256, [vc.ptr(d), vc.ptr(d), vc.ptr(d), vc.i32(1 << 18)]) == 0\n"
+               "assert vc.vcDeviceSynchronize() == 0\n"
+               "assert vc.vcShutdown() == 0\n", {"VC_PROFILE": "1"})
+    assert r.returncode == 0, r.stderr
+    assert "vc profile:" in r.stderr and "vadd" in r.stderr and "memcpy H2D" in r.stderr
+
+
+def test_sync_timeout_returns_not_ready(gpu):
+    """VC_SYNC_TIMEOUT_MS bounds host waits: a deadline shorter than the queued
+    work returns NotReady (the work completes afterwards)."""
+    r = _child("from vkcuda_b200 import vc\n"
+               "assert vc.vcInit() == 0\n"
+               "n = 1 << 28\n"
+               "e, a = vc.vcMalloc(4 * n); e, c = vc.vcMalloc(4 * n)\n"
+               "assert vc.vcMemsetAsync(a, 0, 4 * n) == 0\n"
+               "for _ in range(40):\n"
+               "    assert vc.vadd_f32(a, a, c, n) == 0\n"
+               "r1 = int(vc.vcStreamSynchronize(None))\n"
+               "import time\n"
+               "for _ in range(2000):\n"
+               "    if int(vc.vcStreamSynchronize(None)) == 0: break\n"
+               "    time.sleep(0.005)\n"
+               "r2 = int(vc.vcStreamSynchronize(None))\n"
+               "print(r1, r2)\n", {"VC_SYNC_TIMEOUT_MS": "1"})
+    assert r.returncode == 0, r.stderr
+    r1, r2 = (int(x) for x in r.stdout.split())
+    assert r1 == int(gpu.VCError.NotReady) and r2 == 0
+
+
+def test_multigpu_demo_semantics(gpu, dev):
+    """test/multigpu.vc on two devices: pattern 1000+i on device 0, peer copy
+    0 -> 1, a launch on device 1 writes 2000+i, and a device-1 buffer is freed
+    while device 0 is current. Skipped with one device (the reference then
+    degrades to a 0 -> 0 copy, covered above)."""
+    err, n = gpu.vcGetDeviceCount()
+    if n < 2:
+        pytest.skip("needs two devices")
+    count = 1024
+    pat = (1000 + np.arange(count)).astype(np.float32)
+    src = dev.put(pat)                                       # on device 0
+    assert gpu.vcSetDevice(1) == 0
+    err, dst = gpu.vcMalloc(4 * count)
+    err, two = gpu.vcMalloc(4 * count)
+    assert gpu.vcMemcpyPeer(dst, 1, src.ptr, 0, 4 * count) == 0
+    back = np.empty(count, np.float32)
+    assert gpu.vcMemcpy(back, dst, 4 * count, gpu.VCMemcpyKind.DeviceToHost) == 0
+    assert np.array_equal(back, pat)
+    ones = np.full(count, 1000.0, np.float32)
+    assert gpu.vcMemcpy(two, ones, 4 * count, gpu.VCMemcpyKind.HostToDevice) == 0
+    assert gpu.vadd_f32(dst, two, dst, count) == 0             # launch on device 1
+    assert gpu.vcDeviceSynchronize() == 0
+    assert gpu.vcMemcpy(back, dst, 4 * count, gpu.VCMemcpyKind.DeviceToHost) == 0
+    assert np.array_equal(back, (2000 + np.arange(count)).astype(np.float32))
+    assert gpu.vcSetDevice(0) == 0
+    assert gpu.vcFree(dst) == 0 and gpu.vcFree(two) == 0      # device-1 buffers, device 0 current

@@ -1647,6 +1647,11 @@ int vc_launch_kernel_2d_s(void *k, unsigned gx, unsigned gy, unsigned bx, unsign
   return E(vcLaunchKernel2DS(static_cast<VCKernelHandle>(k), gx, gy, bx, by,
                              reinterpret_cast<const VCKernelArg *>(args), n, S(s)));
 }
+int vc_launch_kernel_indirect_s(void *k, void *ind, size_t offset, unsigned bx, unsigned by,
+                                unsigned bz, const vc_kernel_arg *args, int n, void *s) {
+  return E(vcLaunchKernelIndirectS(static_cast<VCKernelHandle>(k), ind, offset, bx, by, bz,
+                                   reinterpret_cast<const VCKernelArg *>(args), n, S(s)));
+}
 const char *vc_error_string(int err) {
   if (err < 0 || err > static_cast<int>(VCError::Unknown)) return "unknown error";
   return vcErrorString(static_cast<VCError>(err));

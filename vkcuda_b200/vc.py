@@ -131,6 +131,8 @@ SIGNATURES = {
     "vc_launch_kernel": (_I, [_VP, _U, _U, ctypes.POINTER(VCKernelArg), _I]),
     "vc_launch_kernel_s": (_I, [_VP, _U, _U, ctypes.POINTER(VCKernelArg), _I, _VP]),
     "vc_launch_kernel_2d_s": (_I, [_VP, _U, _U, _U, _U, ctypes.POINTER(VCKernelArg), _I, _VP]),
+    "vc_launch_kernel_indirect_s": (_I, [_VP, _VP, _SZ, _U, _U, _U, ctypes.POINTER(VCKernelArg),
+                                         _I, _VP]),
     "vc_error_string": (ctypes.c_char_p, [_I]),
     "vc_get_kernel": (_I, [ctypes.c_char_p, _PVP]),
     "vc_kernel_set_constant": (_I, [_VP, ctypes.c_char_p, _LL]),
@@ -275,14 +277,44 @@ def vcMemsetAsyncS(ptr, value: int, count: int, stream=None) -> VCError:
     return VCError(library().vc_memset_async_s(_addr(ptr), value, count, _stream(stream)))
 
 
+def vcMemsetAsync(ptr, value: int, count: int) -> VCError:
+    """Asynchronous fill on the default stream (reference VCRuntime.h:486)."""
+    return vcMemsetAsyncS(ptr, value, count, None)
+
+
+def vcMemsetS(ptr, value: int, count: int, stream=None) -> VCError:
+    """Fill on `stream`, then wait for it (reference VCRuntime.h:477)."""
+    e = vcMemsetAsyncS(ptr, value, count, stream)
+    return e if e != VCError.Success else vcStreamSynchronize(stream)
+
+
 def vcMemcpy2DAsync(dst, dpitch, src, spitch, width, height, kind, stream=None) -> VCError:
     return VCError(library().vc_memcpy_2d_async(_addr(dst), dpitch, _addr(src), spitch, width,
                                                 height, int(kind), _stream(stream)))
 
 
+def vcMemcpy2DS(dst, dpitch, src, spitch, width, height, kind, stream=None) -> VCError:
+    """2D copy on `stream`, then wait for it (reference VCRuntime.h:496)."""
+    e = vcMemcpy2DAsync(dst, dpitch, src, spitch, width, height, kind, stream)
+    return e if e != VCError.Success else vcStreamSynchronize(stream)
+
+
+def vcMemcpy2D(dst, dpitch, src, spitch, width, height, kind) -> VCError:
+    return vcMemcpy2DS(dst, dpitch, src, spitch, width, height, kind, None)
+
+
 def vcMemset2DAsync(dst, pitch, value, width, height, stream=None) -> VCError:
     return VCError(library().vc_memset_2d_async(_addr(dst), pitch, value, width, height,
                                                 _stream(stream)))
+
+
+def vcMemset2D(dst, pitch, value, width, height) -> VCError:
+    e = vcMemset2DAsync(dst, pitch, value, width, height, None)
+    return e if e != VCError.Success else vcStreamSynchronize(None)
+
+
+def vcMallocHostAsync(nbytes: int, stream=None): return vcMallocHost(nbytes)
+def vcMallocManagedS(nbytes: int, stream=None): return vcMallocManaged(nbytes)
 
 
 def vcDeviceSynchronize() -> VCError: return VCError(library().vc_device_synchronize())
@@ -397,6 +429,34 @@ def vcLaunchKernel2D(kernel, gx: int, gy: int, bx: int, by: int, args, stream=No
     a = _Args(args)
     return VCError(library().vc_launch_kernel_2d_s(kernel, gx, gy, bx, by, a.array, a.count,
                                                    _stream(stream)))
+
+
+def vcLaunchKernelIndirect(kernel, indirect_args, offset: int, block, args, stream=None) -> VCError:
+    """Workgroup counts {x, y, z} are read from the device buffer at `offset`."""
+    bx, by, bz = (tuple(block) + (1, 1))[:3]
+    a = _Args(args)
+    return VCError(library().vc_launch_kernel_indirect_s(kernel, _addr(indirect_args), offset, bx,
+                                                         by, bz, a.array, a.count,
+                                                         _stream(stream)))
+
+
+# Stream-taking forms of the reference header: the functions above already
+# take an optional stream (None = the default stream).
+vcLaunchKernelS = vcLaunchKernel
+vcLaunchKernel2DS = vcLaunchKernel2D
+vcLaunchKernelIndirectS = vcLaunchKernelIndirect
+
+
+def vcLoadKernelFromFile(path: str, entry: str) -> Tuple[VCError, int]:
+    """Load a module from a file (whole 32-bit words) and resolve `entry`."""
+    try:
+        data = open(path, "rb").read()
+    except OSError:
+        return VCError.InvalidValue, 0
+    if len(data) < 4 or len(data) % 4:
+        return VCError.InvalidKernel, 0
+    import struct
+    return vcLoadKernel(list(struct.unpack(f"<{len(data) // 4}I", data)), entry)
 
 
 def vcErrorString(err) -> str:
