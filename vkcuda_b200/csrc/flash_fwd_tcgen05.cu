@@ -411,18 +411,18 @@ bool make_map_bhnd(CUtensorMap *map, bool bf16, const void *base, int BH, int N,
 template <int HD, bool BF16>
 cudaError_t launch_typed(const FlashArgs &f, const CUtensorMap &q, const CUtensorMap &k,
                          const CUtensorMap &v, const CUtensorMap &o, cudaStream_t stream) {
-  static int configured = 0;
+  static uint64_t configured = 0;  // devices whose smem attribute is set
   static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (!(configured & (1 << dev))) {
+    if (dev >= 64 || !(configured & (1ull << dev))) {
       cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<HD, BF16>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)FlashSmem<HD>::kBytes);
       if (e != cudaSuccess) return e;
-      configured |= (1 << dev);
+      if (dev < 64) configured |= (1ull << dev);
     }
   }
   dim3 grid((f.N + 2 * BQ - 1) / (2 * BQ), f.BH);

@@ -565,11 +565,11 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
     cache.valid = true;
   }
 
-  static int configured_device_mask = 0;
+  static uint64_t configured_device_mask = 0;  // devices whose smem attributes are set
   static std::mutex mu;
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (!(configured_device_mask & (1 << dev))) {
+    if (dev >= 64 || !(configured_device_mask & (1ull << dev))) {
       cudaError_t e = cudaFuncSetAttribute(gemm_tcgen05_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)kSmemBytes);
@@ -578,7 +578,7 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kPairSmemBytes);
       if (e != cudaSuccess) return e;
-      configured_device_mask |= (1 << dev);
+      if (dev < 64) configured_device_mask |= (1ull << dev);
     }
   }
   int sms = 148;
