@@ -29,17 +29,27 @@
 //               by more than 2^8; p <= 256 otherwise and the final 1/l makes
 //               it exact), P = exp2(scale_log2 * s - m) rounded to 16 bits,
 //               row sum (of the rounded P for bf16, so numerator and
-//               denominator use the same weights). The softmax is bound by
-//               instruction issue and latency, not by the MUFU exponential
-//               unit: moving a share of the exponentials to an FMA-pipe
-//               polynomial measured slower or equal (scalar: 1/16 -2 %,
-//               1/4 -10 %, 1/2 -25 %; packed f32x2: 1/8 +-1 %, 1/4 -4 %),
-//               so all use MUFU. At the end O / l is staged over the Q tile and
-//               stored with TMA.
+//               denominator use the same weights); one arrival per warp
+//               hands P to the MMA warp (+2.5 % over one per thread). At the
+//               end O / l is staged over the Q tile and stored with TMA.
 // Causal: Q0 of query block b uses key tiles 0..2b, Q1 0..2b+1; blocks are
 // scheduled heaviest first. Keys >= N and keys above the diagonal are masked.
 // Grid: query blocks of one slice are adjacent, so the slices in flight (and
 // their K/V) stay within L2.
+//
+// What bounds it (measured on B200 with clock64 probes): back-to-back
+// tcgen05.mma (M=128, K=16) costs 107 cycles for the S shape (SS, N=128) and
+// 94 for the PV shape (TS, N=128) against 64 at the nominal rate (171 and
+// 138 for N=256; the same per SM for the CTA-pair form; independent of
+// operand layout and data), so a 128-key step of both tiles is >= 3222 MMA
+// cycles; with the softmax removed the kernel runs at that bound, and with
+// it the step measures ~3550 cycles. TMEM is full at d = 128, so neither
+// 256-key S tiles nor Q in TMEM (the cheaper TS form for S) fit. Exponentials
+// on an FMA-pipe polynomial (1/8 .. 1/2 of them) shorten the softmax but slow
+// the concurrent MMAs more (net -1 .. -25 %); two warpgroups taking turns on
+// MUFU measured -1.5 %; a persistent variant (items from an atomic counter,
+// next item's S under the current epilogue) measured -1 % causal, -5 % at
+// N = 16384 causal, +2 % non-causal.
 // Roofline: 4*BH*N^2*d FLOP (2*BH*N^2*d causal) against the dense tensor peak.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -129,7 +139,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
     }
     for (int w = 0; w < 2; ++w) {
       mbar_init(&bars->s_full[w], 1);
-      mbar_init(&bars->p_full[w], kWgThreads);
+      mbar_init(&bars->p_full[w], kWgThreads / 32);  // one per warp
       mbar_init(&bars->o_full[w], 1);
     }
     fence_barrier_init();
@@ -256,7 +266,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
     float l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait(&bars->s_full[w], j & 1)) { ok = false; }
+      if (!mbar_wait(&bars->s_full[w], j & 1)) ok = false;
+      // Warp-uniform status: the TMEM accesses below are warp-collective.
+      ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
       const int key0 = j * BKV;
       const bool need_mask = (key0 + BKV > N) || (causal && key0 + BKV - 1 > qb * 2 * BQ + w * BQ);
@@ -344,11 +356,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->p_full[w]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[w]);
       if (!ok) break;
     }
     // Epilogue: O / l -> 16-bit, staged over this tile's Q buffer, TMA store.
-    if (ok && nkv > 0 && mbar_wait(&bars->o_full[w], (nkv - 1) & 1)) {
+    if (__all_sync(0xffffffffu, ok && nkv > 0 && mbar_wait(&bars->o_full[w], (nkv - 1) & 1))) {
       tc_fence_after();
       uint8_t *stage = smem + (w ? L::kQ1 : L::kQ0);
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
