@@ -171,10 +171,16 @@ def check(err, what):
         raise RuntimeError(f"{what} failed with VCError {int(err)}")
 
 
+IDLE_BEFORE_S = 1.0  # every workload starts from an idle GPU (as the peaks were measured)
+
+
 def timed(dist, stream, fn, steps, warmup, sampler=None):
-    """Run fn() warmup times, then time `steps` calls with CUDA events on
-    `stream` between barriers; returns the max over ranks, in ms."""
+    """After IDLE_BEFORE_S seconds idle, run fn() warmup times, then time
+    `steps` calls with CUDA events on `stream` between barriers; returns the
+    max over ranks, in ms."""
     import torch
+    torch.cuda.synchronize()
+    time.sleep(IDLE_BEFORE_S)
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
