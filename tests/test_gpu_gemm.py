@@ -125,6 +125,16 @@ def test_gemm_unaligned_strides_use_simt_path(gpu, dev, orc):
     _run_gemm(gpu, dev, orc, 65, 33, 37, False, True, lda=37, ldb=33, ldd=33, seed=9)
 
 
+def test_gemm_grouped_tile_order_large_b(gpu, dev, orc):
+    """B of 4608 x 8192 fp16 (72 MiB) exceeds the size above which the pair
+    kernel orders its tiles in groups of 8 pair rows; M = 2304 is 9 pair
+    rows, so the last group is partial. Rows of the partial group and the
+    first group are checked against the oracle."""
+    M, N, K = 2304, 8192, 4608
+    _run_gemm(gpu, dev, orc, M, N, K, False, True, seed=77, rows=(2240, 2304))
+    _run_gemm(gpu, dev, orc, M, N, K, True, True, seed=78, rows=(0, 48))
+
+
 def test_gemm_4096_sampled_rows_and_column_sums(gpu, dev, orc):
     M = N = K = 4096
     got = _run_gemm(gpu, dev, orc, M, N, K, False, True, seed=42, rows=(4000, 4096))

@@ -49,7 +49,11 @@
 // the concurrent MMAs more (net -1 .. -25 %); two warpgroups taking turns on
 // MUFU measured -1.5 %; a persistent variant (items from an atomic counter,
 // next item's S under the current epilogue) measured -1 % causal, -5 % at
-// N = 16384 causal, +2 % non-causal.
+// N = 16384 causal, +2 % non-causal (traced: each warpgroup still waits for
+// its last PV and runs its own epilogue at every item boundary, and short
+// items bring the two warpgroups into phase on MUFU); issuing the first
+// loads before the CTA-wide barrier, with S0(0) waiting on Q0 alone,
+// measured -1 %.
 // Roofline: 4*BH*N^2*d FLOP (2*BH*N^2*d causal) against the dense tensor peak.
 #include <cuda.h>
 #include <cuda_bf16.h>
