@@ -174,10 +174,11 @@ def check(err, what):
 IDLE_BEFORE_S = 1.0  # every workload starts from an idle GPU (as the peaks were measured)
 
 
-def timed(dist, stream, fn, steps, warmup, sampler=None):
+def timed(dist, stream, fn, steps, warmup, sampler=None, stats=None):
     """After IDLE_BEFORE_S seconds idle, run fn() warmup times, then time
     `steps` calls with CUDA events on `stream` between barriers; returns the
-    max over ranks, in ms."""
+    max over ranks, in ms. With `stats` (a dict), an event between steps also
+    gives this rank's median and best step time (`median_ms`, `best_ms`)."""
     import torch
     torch.cuda.synchronize()
     time.sleep(IDLE_BEFORE_S)
@@ -186,17 +187,20 @@ def timed(dist, stream, fn, steps, warmup, sampler=None):
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     ctx = sampler if sampler is not None else _Null()
     with ctx:
-        e0.record(stream)
-        for _ in range(steps):
+        events[0].record(stream)
+        for i in range(steps):
             fn()
-        e1.record(stream)
+            events[i + 1].record(stream)
         torch.cuda.synchronize()
     dist.barrier()
-    return dist.max(e0.elapsed_time(e1))
+    if stats is not None:
+        per = [events[i].elapsed_time(events[i + 1]) for i in range(steps)]
+        stats["median_ms"] = round(statistics.median(per), 4)
+        stats["best_ms"] = round(min(per), 4)
+    return dist.max(events[0].elapsed_time(events[-1]))
 
 
 class _Null:
@@ -241,7 +245,8 @@ def gemm_workload(vc, dist, steps, warmup, pk, device_uuid, want_e2e=True):
         raise RuntimeError(f"GEMM parity guard failed: max err {err}")
 
     sampler = ClockSampler(device_uuid)
-    ms = timed(dist, stream, step, steps, warmup, sampler)
+    step_stats = {}
+    ms = timed(dist, stream, step, steps, warmup, sampler, stats=step_stats)
     flop_step = 2.0 * N ** 3 * GEMMS_PER_STEP
     per_launch_ms = ms / (steps * GEMMS_PER_STEP)
     value = flop_step * steps * dist.world / (ms * 1e-3) / 1e12
@@ -253,6 +258,7 @@ def gemm_workload(vc, dist, steps, warmup, pk, device_uuid, want_e2e=True):
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s",
         "ms_per_step": round(ms / steps, 4),
+        "ms_per_step_median": step_stats["median_ms"], "ms_per_step_best": step_stats["best_ms"],
         "per_launch_ms": round(per_launch_ms, 5),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
@@ -380,7 +386,8 @@ def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk,
     tol = {vc.Dtype.F16: 2e-3, vc.Dtype.BF16: 1e-2, vc.Dtype.F32: 1e-4}[dtype]
     if not perr <= tol:
         raise RuntimeError(f"{name} parity guard failed: {perr}")
-    ms = timed(dist, stream, step, steps, warmup)
+    step_stats = {}
+    ms = timed(dist, stream, step, steps, warmup, stats=step_stats)
     flop = (2.0 if causal else 4.0) * BH * N * N * d  # whole job
     per_launch = ms / steps
     value = flop / (per_launch * 1e-3) / 1e12 if shard_bh else flop * dist.world / (per_launch * 1e-3) / 1e12
@@ -389,7 +396,8 @@ def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk,
     long_kernel = per_launch > 10.0 or ms > 200.0
     peak = pk["bf16_sustained"] if long_kernel else pk["bf16"]
     res = {"workload": name, "value": round(value, 2), "unit": "TFLOP/s",
-           "ms_per_step": round(per_launch, 4),
+           "ms_per_step": round(per_launch, 4), "ms_per_step_median": step_stats["median_ms"],
+           "ms_per_step_best": step_stats["best_ms"],
            "scaling": "strong" if shard_bh else "weak",
            "config": {"B": B, "H": H, "N": N, "d": d, "causal": causal,
                       "dtype": {1: "f16", 2: "bf16", 0: "f32"}[int(dtype)],
@@ -445,6 +453,8 @@ def stream_workload(vc, dist, steps, warmup, pk):
     ms_fused = timed(dist, stream, fused, steps, warmup)
     ms_vadd = timed(dist, stream, vadd_only, steps, warmup)
     ms_sum = timed(dist, stream, sum_only, steps, warmup)
+    # The all-reduce of the fp64 partial on its own (ranks > 1).
+    ms_ar = timed(dist, stream, lambda: dist.pg.all_reduce(part), steps, warmup) if dist.pg else None
     per = ms_fused / steps
     gbs = 12.0 * n_total / (per * 1e-3) / 1e9
     local_gbs = 12.0 * n / (per * 1e-3) / 1e9
@@ -462,6 +472,7 @@ def stream_workload(vc, dist, steps, warmup, pk):
                                 "pair_gbs_16B": round(pair_gbs, 1),
                                 "vadd_frac": round(vadd_gbs / pk["hbm"], 4),
                                 "sum_frac": round(sum_gbs / pk["hbm"], 4)},
+           "allreduce_us": round(ms_ar / steps * 1e3, 2) if ms_ar is not None else None,
            "gpu_launches": steps, "sum_check_rel_err": abs(total - ref.item()) / abs(ref.item())}
     del a, b, c
     torch.cuda.empty_cache()
@@ -544,7 +555,7 @@ def main():
     head = gemm_workload(vc, dist, args.steps, args.warmup, pk, uuid) if "gemm" in only else None
     also = []
     jobs = [("fa_causal", lambda: flash_workload(vc, dist, "fa_causal", 8, 16, 4096, 128, True,
-                                                 vc.Dtype.F16, max(args.steps, 10), args.warmup, pk,
+                                                 vc.Dtype.F16, max(args.steps, 20), args.warmup, pk,
                                                  shard_bh=False)),
             ("fa_bf16", lambda: flash_workload(vc, dist, "fa_bf16", 32, 32, 8192, 128, False,
                                                vc.Dtype.BF16, max(3, min(args.steps, 5)),

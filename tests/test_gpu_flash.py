@@ -81,6 +81,26 @@ def test_flash_f32_vs_oracle(gpu, dev, orc, BH, N, d, causal):
     assert np.abs(do.to_host(np.float32, Q.size) - ref).max() <= TOL["f32"]
 
 
+@pytest.mark.parametrize("BH,N,d,causal", [(8, 1024, 64, True), (4, 2048, 128, False),
+                                           (16, 520, 24, False)])
+def test_flash_f32_large_grid_vs_oracle(gpu, dev, orc, BH, N, d, causal):
+    """Grids that fill the GPU take the 8-rows-per-block variant; checked on
+    the first and last slices, first and last 40 rows."""
+    rng = np.random.default_rng(BH * N + d + 1)
+    Q, K, V = (rng.standard_normal(BH * N * d).astype(np.float32) for _ in range(3))
+    s = np.float32(LOG2E / math.sqrt(d))
+    dq, dk, dv, do = dev.put(Q), dev.put(K), dev.put(V), dev.alloc(Q.nbytes)
+    assert gpu.flash_fwd(dq.ptr, dk.ptr, dv.ptr, do.ptr, BH, N, d, s, causal, gpu.Dtype.F32) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    got = do.to_host(np.float32, Q.size).reshape(BH, N, d)
+    for bh in ((0, 1), (BH - 1, BH)):
+        for rows in ((0, 40), (N - 40, N)):
+            ref = orc.attention(Q, K, V, BH, N, d, s, causal, bh_range=bh,
+                                row_range=rows).reshape(BH, N, d)
+            err = np.abs(got[bh[0]:bh[1], rows[0]:rows[1]] - ref[bh[0]:bh[1], rows[0]:rows[1]]).max()
+            assert err <= TOL["f32"], (bh, rows, err)
+
+
 def _run_tc(gpu, dev, orc, BH, N, d, causal, bf16, seed=0, scale_in=1.0, bh_check=None,
             row_check=None, qk_scale=1.0):
     rng = np.random.default_rng(seed)

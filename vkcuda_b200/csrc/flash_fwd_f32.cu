@@ -4,64 +4,127 @@
 // causal mask key j > query i) and for the fp32 benchmark config.
 //
 // The reference gives one thread a whole query row. Here a row is split over
-// 16 lanes (each takes every 16th key of a 32-key tile held in shared
-// memory), every lane keeps its own running max / sum / accumulator in fp32,
-// and the 16 partial states are merged with shuffles at the end:
+// kLanes lanes of a warp (lane l takes keys l, l + kLanes, ... of each key
+// tile), every lane keeps its own running max / sum / accumulator in fp32,
+// and the partial states are merged with shuffles at the end:
 //   m = max(m_a, m_b), l = l_a 2^(m_a-m) + l_b 2^(m_b-m), acc likewise.
-// 8 rows per 128-thread block; any head dimension d <= 128. exp2f is the
-// accurate CUDA function, so the result tracks an fp64 evaluation to ~1e-6
-// for unit-variance inputs.
+// Any head dimension d <= 128. K/V tiles (64 keys; 32 at d > 64, halving the
+// shared memory) are double-buffered in shared memory with cp.async,
+// so the load of tile t+1 overlaps the arithmetic on tile t. Small grids
+// (the 1 x 256 x 64 demo shape is 16.8 MFLOP, latency-bound) run 4 rows of
+// 32 lanes per block, for more blocks; grids that fill the GPU run 8 rows of
+// 16 lanes, so that each staged K/V element serves twice the rows in a block
+// of the same 128 threads. exp2f is the accurate CUDA function, so
+// the result tracks an fp64 evaluation to ~1e-6 for unit-variance inputs.
 #include <cuda_runtime.h>
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 
 #include "internal.h"
 
 namespace vcb {
 namespace {
 
-constexpr int kRows = 8, kSplit = 16, kKeyTile = 32;
+
+__device__ __forceinline__ void cp_async4(float *smem_dst, const float *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Shared memory: Q rows, then two K buffers and two V buffers of kKeyTile
+// keys; rows padded to D + 1 floats so that the 32 lanes reading 32
+// different keys of one column hit 32 different banks.
+template <int D, int kRows, int kLanes>
+struct F32Smem {
+  static constexpr int kKeyTile = D > 64 ? 32 : 64;
+  static constexpr int kThreads = kRows * kLanes;
+  static constexpr int kPitch = D + 1;
+  static constexpr size_t kQ = 0;
+  static constexpr size_t kK = kQ + size_t(kRows) * kPitch;
+  static constexpr size_t kV = kK + 2 * size_t(kKeyTile) * kPitch;
+  static constexpr size_t kFloats = kV + 2 * size_t(kKeyTile) * kPitch;
+  static constexpr size_t kBytes = kFloats * sizeof(float);
+};
 
 // D is the compile-time capacity; the head dimension d <= D is a launch
 // argument (columns d..D-1 of the staged tiles are zero, so they add nothing).
-template <int D>
-__global__ void __launch_bounds__(kRows *kSplit)
+template <int D, int kRows, int kLanes>
+__global__ void __launch_bounds__(kRows * kLanes)
 flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
                  const float *__restrict__ V, float *__restrict__ O, int N, int d,
                  float scale_log2, int causal) {
-  __shared__ float Qs[kRows][D + 1];
-  __shared__ float Ks[kKeyTile][D + 1];
-  __shared__ float Vs[kKeyTile][D + 1];
+  using L = F32Smem<D, kRows, kLanes>;
+  constexpr int kKeyTile = L::kKeyTile, kThreads = L::kThreads;
+  extern __shared__ float fsm[];
+  float *Qs = fsm + L::kQ;
   const int64_t base = static_cast<int64_t>(blockIdx.y) * N * d;
   const int q0 = blockIdx.x * kRows;
-  const int r = threadIdx.x / kSplit, sp = threadIdx.x % kSplit;
+  const int r = threadIdx.x / kLanes, lane = threadIdx.x % kLanes;
   const int qi = q0 + r;
 
-  for (int i = threadIdx.x; i < kRows * D; i += blockDim.x) {
+  for (int i = threadIdx.x; i < kRows * D; i += kThreads) {
     const int rr = i / D, dd = i % D;
-    Qs[rr][dd] = (q0 + rr < N && dd < d) ? Q[base + static_cast<int64_t>(q0 + rr) * d + dd] : 0.0f;
+    Qs[rr * L::kPitch + dd] =
+        (q0 + rr < N && dd < d) ? Q[base + static_cast<int64_t>(q0 + rr) * d + dd] : 0.0f;
   }
+  // Stage key tile t (keys t*64 ..) into buffer b: cp.async for elements in
+  // range, zeros (plain stores) elsewhere.
+  auto stage = [&](int t, int b) {
+    float *Kb = fsm + L::kK + size_t(b) * kKeyTile * L::kPitch;
+    float *Vb = fsm + L::kV + size_t(b) * kKeyTile * L::kPitch;
+    const int k0 = t * kKeyTile;
+    for (int i = threadIdx.x; i < kKeyTile * D; i += kThreads) {
+      const int rr = i / D, dd = i % D;
+      float *kd = Kb + rr * L::kPitch + dd, *vd = Vb + rr * L::kPitch + dd;
+      if (k0 + rr < N && dd < d) {
+        const int64_t off = base + static_cast<int64_t>(k0 + rr) * d + dd;
+        cp_async4(kd, K + off);
+        cp_async4(vd, V + off);
+      } else {
+        *kd = 0.0f;
+        *vd = 0.0f;
+      }
+    }
+    cp_async_commit();
+  };
+
   float m = -INFINITY, l = 0.0f, acc[D];
 #pragma unroll
   for (int dd = 0; dd < D; ++dd) acc[dd] = 0.0f;
 
   const int kend = causal ? min(N, q0 + kRows) : N;
-  for (int k0 = 0; k0 < kend; k0 += kKeyTile) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < kKeyTile * D; i += blockDim.x) {
-      const int rr = i / D, dd = i % D;
-      const bool in = (k0 + rr < N) && dd < d;
-      const int64_t off = base + static_cast<int64_t>(k0 + rr) * d + dd;
-      Ks[rr][dd] = in ? K[off] : 0.0f;
-      Vs[rr][dd] = in ? V[off] : 0.0f;
+  const int ntiles = (kend + kKeyTile - 1) / kKeyTile;
+  if (ntiles > 0) stage(0, 0);
+  for (int t = 0; t < ntiles; ++t) {
+    if (t + 1 < ntiles) {
+      stage(t + 1, (t + 1) & 1);
+      cp_async_wait<1>();  // this thread's copies of tile t have landed
+    } else {
+      cp_async_wait<0>();
     }
-    __syncthreads();
-    for (int jj = sp; jj < kKeyTile; jj += kSplit) {
-      const int j = k0 + jj;
+    __syncthreads();  // everyone's copies and zero fills of tile t (and Q) visible
+    const float *Kb = fsm + L::kK + size_t(t & 1) * kKeyTile * L::kPitch;
+    const float *Vb = fsm + L::kV + size_t(t & 1) * kKeyTile * L::kPitch;
+    const float *qrow = Qs + r * L::kPitch;
+#pragma unroll
+    for (int h = 0; h < kKeyTile / kLanes; ++h) {
+      const int jj = lane + h * kLanes;
+      const int j = t * kKeyTile + jj;
       if (j >= N || (causal && j > qi)) continue;
+      const float *krow = Kb + jj * L::kPitch;
       float dot = 0.0f;
 #pragma unroll
-      for (int dd = 0; dd < D; ++dd) dot = fmaf(Qs[r][dd], Ks[jj][dd], dot);
+      for (int dd = 0; dd < D; ++dd) dot = fmaf(qrow[dd], krow[dd], dot);
       const float s = dot * scale_log2;
       if (s > m) {
         const float alpha = exp2f(m - s);  // 0 when m = -inf
@@ -72,13 +135,15 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
       }
       const float p = exp2f(s - m);
       l += p;
+      const float *vrow = Vb + jj * L::kPitch;
 #pragma unroll
-      for (int dd = 0; dd < D; ++dd) acc[dd] = fmaf(p, Vs[jj][dd], acc[dd]);
+      for (int dd = 0; dd < D; ++dd) acc[dd] = fmaf(p, vrow[dd], acc[dd]);
     }
+    __syncthreads();  // buffer t & 1 is refilled by the stage() of iteration t + 1
   }
-  // Merge the 16 lane states of the row (lanes of a row are consecutive).
+  // Merge the kLanes lane states of the row (consecutive lanes of a warp).
 #pragma unroll
-  for (int off = kSplit / 2; off > 0; off >>= 1) {
+  for (int off = kLanes / 2; off > 0; off >>= 1) {
     const float m_o = __shfl_xor_sync(0xffffffffu, m, off);
     const float l_o = __shfl_xor_sync(0xffffffffu, l, off);
     const float mn = fmaxf(m, m_o);
@@ -96,30 +161,61 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
     const float inv = 1.0f / l;
 #pragma unroll
     for (int dd = 0; dd < D; ++dd)
-      if (dd % kSplit == sp && dd < d) O[base + static_cast<int64_t>(qi) * d + dd] = acc[dd] * inv;
+      if (dd % kLanes == lane && dd < d) O[base + static_cast<int64_t>(qi) * d + dd] = acc[dd] * inv;
   }
+}
+
+template <int D, int kRows, int kLanes>
+cudaError_t launch_dr(const FlashArgs &f, cudaStream_t stream) {
+  using L = F32Smem<D, kRows, kLanes>;
+  static uint64_t configured = 0;  // devices whose smem attribute is set
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 64 || !(configured & (1ull << dev))) {
+      cudaError_t e = cudaFuncSetAttribute(flash_f32_kernel<D, kRows, kLanes>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)L::kBytes);
+      if (e != cudaSuccess) return e;
+      if (dev < 64) configured |= (1ull << dev);
+    }
+  }
+  dim3 grid((f.N + kRows - 1) / kRows, f.BH);
+  flash_f32_kernel<D, kRows, kLanes><<<grid, L::kThreads, L::kBytes, stream>>>(
+      static_cast<const float *>(f.Q), static_cast<const float *>(f.K),
+      static_cast<const float *>(f.V), static_cast<float *>(f.O), f.N, f.d, f.scale_log2,
+      f.causal ? 1 : 0);
+  return cudaGetLastError();
+}
+
+// 4 rows of 32 lanes while 8-row blocks would not give every SM two of them,
+// else 8 rows of 16 lanes.
+template <int D>
+cudaError_t launch_d(const FlashArgs &f, cudaStream_t stream) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms <= 0)
+      sms = 148;
+  }
+  const long long blocks8 = (long long)f.BH * ((f.N + 7) / 8);
+  return blocks8 >= 2LL * sms ? launch_dr<D, 8, 16>(f, stream) : launch_dr<D, 4, 32>(f, stream);
 }
 
 }  // namespace
 
 cudaError_t launch_flash_fwd_f32(const FlashArgs &f, cudaStream_t stream) {
   if (f.BH <= 0 || f.N <= 0 || f.BH > 65535) return cudaErrorInvalidValue;
-  dim3 grid((f.N + kRows - 1) / kRows, f.BH);
-  const float *Q = static_cast<const float *>(f.Q), *K = static_cast<const float *>(f.K),
-              *V = static_cast<const float *>(f.V);
-  float *O = static_cast<float *>(f.O);
-  const int c = f.causal ? 1 : 0;
   // Smallest compiled capacity that holds d.
   if (f.d <= 0 || f.d > 128) return cudaErrorInvalidValue;
-  if (f.d <= 16)
-    flash_f32_kernel<16><<<grid, kRows * kSplit, 0, stream>>>(Q, K, V, O, f.N, f.d, f.scale_log2, c);
-  else if (f.d <= 32)
-    flash_f32_kernel<32><<<grid, kRows * kSplit, 0, stream>>>(Q, K, V, O, f.N, f.d, f.scale_log2, c);
-  else if (f.d <= 64)
-    flash_f32_kernel<64><<<grid, kRows * kSplit, 0, stream>>>(Q, K, V, O, f.N, f.d, f.scale_log2, c);
-  else
-    flash_f32_kernel<128><<<grid, kRows * kSplit, 0, stream>>>(Q, K, V, O, f.N, f.d, f.scale_log2, c);
-  return cudaGetLastError();
+  if (f.d <= 16) return launch_d<16>(f, stream);
+  if (f.d <= 32) return launch_d<32>(f, stream);
+  if (f.d <= 64) return launch_d<64>(f, stream);
+  return launch_d<128>(f, stream);
 }
 
 }  // namespace vcb
