@@ -9,12 +9,14 @@
 // and the partial states are merged with shuffles at the end:
 //   m = max(m_a, m_b), l = l_a 2^(m_a-m) + l_b 2^(m_b-m), acc likewise.
 // Any head dimension d <= 128. K/V tiles (64 keys; 32 at d > 64, halving the
-// shared memory) are double-buffered in shared memory with cp.async,
-// so the load of tile t+1 overlaps the arithmetic on tile t. Small grids
-// (the 1 x 256 x 64 demo shape is 16.8 MFLOP, latency-bound) run 4 rows of
-// 32 lanes per block, for more blocks; grids that fill the GPU run 8 rows of
-// 16 lanes, so that each staged K/V element serves twice the rows in a block
-// of the same 128 threads. exp2f is the accurate CUDA function, so
+// shared memory) stream through a ring of kStages shared-memory buffers
+// filled by cp.async, so the loads of the next tiles overlap the arithmetic
+// on the current one. Small grids (the 1 x 256 x 64 demo shape is 16.8
+// MFLOP, latency-bound) run 4 rows of 32 lanes per block, for more blocks,
+// with a 4-deep ring (all of a 256-key sequence in flight at once); grids
+// that fill the GPU run 8 rows of 16 lanes, so that each staged K/V element
+// serves twice the rows in a block of the same 128 threads, with a 2-deep
+// ring so that several blocks share an SM. exp2f is the accurate CUDA function, so
 // the result tracks an fp64 evaluation to ~1e-6 for unit-variance inputs.
 #include <cuda_runtime.h>
 #include <cmath>
@@ -41,29 +43,29 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Shared memory: Q rows, then two K buffers and two V buffers of kKeyTile
-// keys; rows padded to D + 1 floats so that the 32 lanes reading 32
-// different keys of one column hit 32 different banks.
-template <int D, int kRows, int kLanes>
+// Shared memory: Q rows, then kStages K buffers and kStages V buffers of
+// kKeyTile keys; rows padded to D + 1 floats so that the lanes reading
+// different keys of one column hit different banks.
+template <int D, int kRows, int kLanes, int kStages>
 struct F32Smem {
   static constexpr int kKeyTile = D > 64 ? 32 : 64;
   static constexpr int kThreads = kRows * kLanes;
   static constexpr int kPitch = D + 1;
   static constexpr size_t kQ = 0;
   static constexpr size_t kK = kQ + size_t(kRows) * kPitch;
-  static constexpr size_t kV = kK + 2 * size_t(kKeyTile) * kPitch;
-  static constexpr size_t kFloats = kV + 2 * size_t(kKeyTile) * kPitch;
+  static constexpr size_t kV = kK + kStages * size_t(kKeyTile) * kPitch;
+  static constexpr size_t kFloats = kV + kStages * size_t(kKeyTile) * kPitch;
   static constexpr size_t kBytes = kFloats * sizeof(float);
 };
 
 // D is the compile-time capacity; the head dimension d <= D is a launch
 // argument (columns d..D-1 of the staged tiles are zero, so they add nothing).
-template <int D, int kRows, int kLanes>
+template <int D, int kRows, int kLanes, int kStages>
 __global__ void __launch_bounds__(kRows * kLanes)
 flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
                  const float *__restrict__ V, float *__restrict__ O, int N, int d,
                  float scale_log2, int causal) {
-  using L = F32Smem<D, kRows, kLanes>;
+  using L = F32Smem<D, kRows, kLanes, kStages>;
   constexpr int kKeyTile = L::kKeyTile, kThreads = L::kThreads;
   extern __shared__ float fsm[];
   float *Qs = fsm + L::kQ;
@@ -77,8 +79,8 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
     Qs[rr * L::kPitch + dd] =
         (q0 + rr < N && dd < d) ? Q[base + static_cast<int64_t>(q0 + rr) * d + dd] : 0.0f;
   }
-  // Stage key tile t (keys t*64 ..) into buffer b: cp.async for elements in
-  // range, zeros (plain stores) elsewhere.
+  // Stage key tile t into buffer b: cp.async for elements in range, zeros
+  // (plain stores) elsewhere; one commit group per tile.
   auto stage = [&](int t, int b) {
     float *Kb = fsm + L::kK + size_t(b) * kKeyTile * L::kPitch;
     float *Vb = fsm + L::kV + size_t(b) * kKeyTile * L::kPitch;
@@ -104,17 +106,22 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
 
   const int kend = causal ? min(N, q0 + kRows) : N;
   const int ntiles = (kend + kKeyTile - 1) / kKeyTile;
-  if (ntiles > 0) stage(0, 0);
+  // Tiles 0 .. kStages-2 up front; every iteration adds one more (or an empty
+  // group past the end), so "all but the newest kStages-1 groups complete"
+  // means tile t has landed.
+#pragma unroll
+  for (int t = 0; t < kStages - 1; ++t) {
+    if (t < ntiles) stage(t, t);
+    else cp_async_commit();
+  }
   for (int t = 0; t < ntiles; ++t) {
-    if (t + 1 < ntiles) {
-      stage(t + 1, (t + 1) & 1);
-      cp_async_wait<1>();  // this thread's copies of tile t have landed
-    } else {
-      cp_async_wait<0>();
-    }
+    const int ahead = t + kStages - 1;
+    if (ahead < ntiles) stage(ahead, ahead % kStages);
+    else cp_async_commit();
+    cp_async_wait<kStages - 1>();  // this thread's copies of tile t have landed
     __syncthreads();  // everyone's copies and zero fills of tile t (and Q) visible
-    const float *Kb = fsm + L::kK + size_t(t & 1) * kKeyTile * L::kPitch;
-    const float *Vb = fsm + L::kV + size_t(t & 1) * kKeyTile * L::kPitch;
+    const float *Kb = fsm + L::kK + size_t(t % kStages) * kKeyTile * L::kPitch;
+    const float *Vb = fsm + L::kV + size_t(t % kStages) * kKeyTile * L::kPitch;
     const float *qrow = Qs + r * L::kPitch;
 #pragma unroll
     for (int h = 0; h < kKeyTile / kLanes; ++h) {
@@ -139,7 +146,7 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
 #pragma unroll
       for (int dd = 0; dd < D; ++dd) acc[dd] = fmaf(p, vrow[dd], acc[dd]);
     }
-    __syncthreads();  // buffer t & 1 is refilled by the stage() of iteration t + 1
+    __syncthreads();  // buffer t % kStages is refilled by the stage() of iteration t + 1
   }
   // Merge the kLanes lane states of the row (consecutive lanes of a warp).
 #pragma unroll
@@ -165,9 +172,9 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
   }
 }
 
-template <int D, int kRows, int kLanes>
+template <int D, int kRows, int kLanes, int kStages>
 cudaError_t launch_dr(const FlashArgs &f, cudaStream_t stream) {
-  using L = F32Smem<D, kRows, kLanes>;
+  using L = F32Smem<D, kRows, kLanes, kStages>;
   static uint64_t configured = 0;  // devices whose smem attribute is set
   static std::mutex mu;
   int dev = 0;
@@ -175,7 +182,7 @@ cudaError_t launch_dr(const FlashArgs &f, cudaStream_t stream) {
   {
     std::lock_guard<std::mutex> lk(mu);
     if (dev >= 64 || !(configured & (1ull << dev))) {
-      cudaError_t e = cudaFuncSetAttribute(flash_f32_kernel<D, kRows, kLanes>,
+      cudaError_t e = cudaFuncSetAttribute(flash_f32_kernel<D, kRows, kLanes, kStages>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)L::kBytes);
       if (e != cudaSuccess) return e;
@@ -183,7 +190,7 @@ cudaError_t launch_dr(const FlashArgs &f, cudaStream_t stream) {
     }
   }
   dim3 grid((f.N + kRows - 1) / kRows, f.BH);
-  flash_f32_kernel<D, kRows, kLanes><<<grid, L::kThreads, L::kBytes, stream>>>(
+  flash_f32_kernel<D, kRows, kLanes, kStages><<<grid, L::kThreads, L::kBytes, stream>>>(
       static_cast<const float *>(f.Q), static_cast<const float *>(f.K),
       static_cast<const float *>(f.V), static_cast<float *>(f.O), f.N, f.d, f.scale_log2,
       f.causal ? 1 : 0);
@@ -203,7 +210,8 @@ cudaError_t launch_d(const FlashArgs &f, cudaStream_t stream) {
       sms = 148;
   }
   const long long blocks8 = (long long)f.BH * ((f.N + 7) / 8);
-  return blocks8 >= 2LL * sms ? launch_dr<D, 8, 16>(f, stream) : launch_dr<D, 4, 32>(f, stream);
+  return blocks8 >= 2LL * sms ? launch_dr<D, 8, 16, 2>(f, stream)
+                              : launch_dr<D, 4, 32, 4>(f, stream);
 }
 
 }  // namespace
