@@ -32,10 +32,12 @@
 //               denominator use the same weights); one arrival per warp
 //               hands P to the MMA warp (+2.5 % over one per thread). At the
 //               end O / l is staged over the Q tile and stored with TMA.
-// Causal: Q0 of query block b uses key tiles 0..2b, Q1 0..2b+1; blocks are
-// scheduled heaviest first. Keys >= N and keys above the diagonal are masked.
-// Grid: query blocks of one slice are adjacent, so the slices in flight (and
-// their K/V) stay within L2.
+// Causal: Q0 of query block b uses key tiles 0..2b, Q1 0..2b+1. Keys >= N
+// and keys above the diagonal are masked. Blocks are ordered heaviest first
+// across groups of 8 slices (vs heaviest first per slice: +4.6 % at N = 4096,
+// +9.3 % at N = 16384, as the last slices' heavy blocks no longer start at
+// the end of the grid). Non-causal: query blocks of one slice are adjacent.
+// Either way the slices in flight (and their K/V) stay within L2.
 //
 // What bounds it (measured on B200 with clock64 probes): back-to-back
 // tcgen05.mma (M=128, K=16) costs 107 cycles for the S shape (SS, N=128) and
@@ -77,6 +79,7 @@ constexpr int kWgThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kBoxBytes = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kCausalGroup = 8;            // slices per causal ordering group
 
 
 
@@ -128,8 +131,21 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nqb = (N + 2 * BQ - 1) / (2 * BQ);
-  const int qb = causal ? (nqb - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-  const int bh = blockIdx.y;
+  // Block order (blocks are dispatched x-fastest): non-causal, the query
+  // blocks of one slice are adjacent; causal, groups of kCausalGroup slices,
+  // heaviest query block of every slice of the group first, so that the
+  // heavy blocks of the last slices do not start at the end of the grid,
+  // while a group's K/V (8 x 2 MiB at N = 4096) stays in L2.
+  int qb = blockIdx.x, bh = blockIdx.y;
+  if (causal) {
+    const int lin = blockIdx.y * nqb + blockIdx.x;
+    const int g = lin / (kCausalGroup * nqb);
+    const int first = g * kCausalGroup;
+    const int gsz = min(kCausalGroup, (int)gridDim.y - first);
+    const int r = lin - g * kCausalGroup * nqb;
+    qb = nqb - 1 - r / gsz;
+    bh = first + r % gsz;
+  }
   const int kv_all = (N + BKV - 1) / BKV;
   // Key tiles used by Q0 / Q1 (n1 >= n0).
   const int n0 = causal ? min(2 * qb + 1, kv_all) : kv_all;
