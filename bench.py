@@ -581,7 +581,8 @@ def main():
                 "dtype": "f16", "data": "synthetic (seeded U[-1,1) fp16 inputs)",
                 "config": config}
         if head:
-            for key in ("roofline", "clocks", "e2e", "gpu_launches", "per_launch_ms"):
+            for key in ("ms_per_step_median", "ms_per_step_best", "roofline", "clocks", "e2e",
+                        "gpu_launches", "per_launch_ms"):
                 line[key] = head[key]
             line["cpu_baseline"] = base
         line["also"] = also
