@@ -13,7 +13,8 @@ The other benchmark configurations ride along in "also":
   fa_bf16    flash-attention fwd bf16, B=32, H=32, N=8192, d=128, sharded
              over ranks by batch x heads (strong scaling)
   stream     vadd c = a + b then sum(c), n = 2^30 fp32, sharded contiguously
-             over ranks, fp64 partials combined by one NCCL all-reduce
+             over ranks, the ranks' fp64 sums combined inside the kernel over
+             NVLink (an NCCL all-reduce after the kernel is timed beside it)
   fa_f32     flash-attention fwd fp32, B=1, H=1, N=256, d=64 (the demo's
              precision; latency bound)
 Under torchrun (N > 1) ranks time on the device with CUDA events between
@@ -428,12 +429,41 @@ def stream_workload(vc, dist, steps, warmup, pk):
     part = torch.zeros(1, dtype=torch.float64, device="cuda")
     stream = torch.cuda.current_stream()
     cs = stream.cuda_stream
+    # N > 1: the per-GPU sums are combined inside the kernel through the
+    # ranks' mailboxes (NVLink peer stores); the handles travel once over the
+    # process group.
+    boxes = None
+    if dist.pg:
+        err, own = vc.peer_mailbox_alloc()
+        check(err, "vc_peer_mailbox_alloc")
+        err, handle = vc.peer_ipc_get_handle(own)
+        check(err, "vc_peer_ipc_get_handle")
+        handles = [None] * dist.world
+        dist.pg.all_gather_object(handles, handle)
+        boxes = []
+        for i, h in enumerate(handles):
+            if i == dist.rank:
+                boxes.append(own)
+            else:
+                err, ptr = vc.peer_ipc_open(h)
+                check(err, "vc_peer_ipc_open")
+                boxes.append(ptr)
+    epoch = [0]
 
     def fused():
+        if boxes is None:
+            check(vc.vadd_sum_f32(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, part.data_ptr(),
+                                  cs), "vc_vadd_sum_f32")
+            return
+        epoch[0] += 1
+        check(vc.vadd_sum_f32_allreduce(a.data_ptr(), b.data_ptr(), c.data_ptr(), n,
+                                        part.data_ptr(), boxes, dist.rank, epoch[0], cs),
+              "vc_vadd_sum_f32_allreduce")
+
+    def fused_then_nccl():
         check(vc.vadd_sum_f32(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, part.data_ptr(), cs),
               "vc_vadd_sum_f32")
-        if dist.pg:
-            dist.pg.all_reduce(part)
+        dist.pg.all_reduce(part)
 
     def vadd_only():
         check(vc.vadd_f32(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, cs), "vc_vadd_f32")
@@ -453,8 +483,18 @@ def stream_workload(vc, dist, steps, warmup, pk):
     ms_fused = timed(dist, stream, fused, steps, warmup)
     ms_vadd = timed(dist, stream, vadd_only, steps, warmup)
     ms_sum = timed(dist, stream, sum_only, steps, warmup)
-    # The all-reduce of the fp64 partial on its own (ranks > 1).
+    # For comparison (ranks > 1): the kernel followed by an NCCL all-reduce of
+    # the partial, and that all-reduce on its own.
+    ms_nccl = timed(dist, stream, fused_then_nccl, steps, warmup) if dist.pg else None
     ms_ar = timed(dist, stream, lambda: dist.pg.all_reduce(part), steps, warmup) if dist.pg else None
+    if boxes is not None:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank stores into a mailbox after this
+        for i, ptr in enumerate(boxes):
+            if i != dist.rank:
+                check(vc.peer_ipc_close(ptr), "vc_peer_ipc_close")
+        dist.barrier()
+        check(vc.peer_mailbox_free(boxes[dist.rank]), "vc_peer_mailbox_free")
     per = ms_fused / steps
     gbs = 12.0 * n_total / (per * 1e-3) / 1e9
     local_gbs = 12.0 * n / (per * 1e-3) / 1e9
@@ -464,7 +504,8 @@ def stream_workload(vc, dist, steps, warmup, pk):
     res = {"workload": "stream", "value": round(gbs, 1), "unit": "GB/s",
            "ms_per_step": round(per, 4), "scaling": "strong",
            "config": {"n": n_total, "n_per_rank": n, "dtype": "f32",
-                      "step": "fused vadd+sum kernel, then NCCL all-reduce of the fp64 partial"},
+                      "step": "fused vadd+sum kernel; with N > 1 the per-GPU fp64 sums are "
+                              "combined inside the kernel through NVLink peer stores"},
            "roofline": {"bound": "hbm", "achieved": round(local_gbs, 1), "peak": pk["hbm"],
                         "unit": "GB/s", "frac": round(local_gbs / pk["hbm"], 4),
                         "bytes_per_elem": 12, "traffic": traffic_table().get("stream_fused")},
@@ -473,6 +514,7 @@ def stream_workload(vc, dist, steps, warmup, pk):
                                 "vadd_frac": round(vadd_gbs / pk["hbm"], 4),
                                 "sum_frac": round(sum_gbs / pk["hbm"], 4)},
            "allreduce_us": round(ms_ar / steps * 1e3, 2) if ms_ar is not None else None,
+           "nccl_step_ms": round(ms_nccl / steps, 4) if ms_nccl is not None else None,
            "gpu_launches": steps, "sum_check_rel_err": abs(total - ref.item()) / abs(ref.item())}
     del a, b, c
     torch.cuda.empty_cache()

@@ -189,6 +189,30 @@ int vc_sum_f32_noalloc(const float *x, int64_t n, double *out, void *stream);
 int vc_vadd_sum_f32(const float *a, const float *b, float *c, int64_t n,
                     double *out, void *stream);
 
+/* ---- Cross-GPU sum without a library collective (one process per GPU).
+ * The reference's reduce is single-device (test/reduce.vc); its multi-GPU
+ * form here combines the per-GPU partials, which a library all-reduce would
+ * otherwise do after the kernel, inside the sum kernel itself over NVLink:
+ * each rank allocates one mailbox (vc_peer_mailbox_alloc), exports it
+ * (vc_peer_ipc_get_handle), imports every other rank's
+ * (vc_peer_ipc_open, handles exchanged by any host channel), and passes
+ * all `world` mailbox addresses, in rank order with its own at `rank`, to
+ * vc_vadd_sum_f32_allreduce. That kernel writes c = a + b, and *out = the
+ * sum over all ranks of sum(c): its last block stores this GPU's sum into
+ * every mailbox with peer stores, then waits for the other ranks' (bounded:
+ * after 2 s it gives NaN and records a timeout, see vc_kernel_error). Every
+ * rank must make the same sequence of calls with the same increasing
+ * `epoch` (>= 1), one per call. world <= 8. */
+#define VC_IPC_HANDLE_BYTES 64
+int vc_peer_mailbox_alloc(void **mailbox);
+int vc_peer_mailbox_free(void *mailbox);
+int vc_peer_ipc_get_handle(const void *dev_ptr, void *handle /* VC_IPC_HANDLE_BYTES */);
+int vc_peer_ipc_open(const void *handle, void **dev_ptr);
+int vc_peer_ipc_close(void *dev_ptr);
+int vc_vadd_sum_f32_allreduce(const float *a, const float *b, float *c, int64_t n,
+                              double *out, void *const *mailboxes, int rank, int world,
+                              unsigned long long epoch, void *stream);
+
 /* Demo block reduce: out[g] = tree sum of in[g*block .. g*block+block) with
  * the reference's pairing order (test/reduce.vc:11-38), for g < groups. */
 int vc_block_reduce_f32(const float *in, float *out, int n, int block,

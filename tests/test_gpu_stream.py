@@ -126,3 +126,69 @@ def test_native_sum_through_registry(gpu, dev, orc):
     assert gpu.vcDeviceSynchronize() == 0
     assert _read_f64(dout) == pytest.approx(orc.sum_f64(x), rel=SUM_RTOL)
     gpu.vcReleaseKernel(k)
+
+
+# ---- cross-GPU sum through mailboxes (vc_vadd_sum_f32_allreduce)
+def test_allreduce_one_rank_equals_fused_sum(gpu, dev, orc):
+    """world = 1: the exchange runs against this GPU's own mailbox and gives
+    the fused sum; consecutive epochs alternate the two slots."""
+    n = (1 << 20) + 5
+    rng = np.random.default_rng(11)
+    a = rng.random(n, dtype=np.float32)
+    b = rng.random(n, dtype=np.float32)
+    da, db, dc, dout = dev.put(a), dev.put(b), dev.alloc(4 * n), dev.alloc(8)
+    err, mb = gpu.peer_mailbox_alloc()
+    assert err == 0 and mb
+    try:
+        ref = orc.sum_f64(orc.vadd(a, b))
+        for epoch in (1, 2, 3):
+            assert gpu.vadd_sum_f32_allreduce(da.ptr, db.ptr, dc.ptr, n, dout.ptr, [mb], 0,
+                                              epoch) == 0
+            assert gpu.vcDeviceSynchronize() == 0
+            got = float(dout.to_host(np.float64, 1)[0])
+            assert abs(got - ref) <= SUM_RTOL * abs(ref)
+        assert np.array_equal(dc.to_host(np.float32, n), orc.vadd(a, b))
+        assert gpu.kernel_error(True) == 0
+    finally:
+        gpu.peer_mailbox_free(mb)
+
+
+def test_allreduce_silent_peer_times_out(gpu, dev):
+    """A rank whose peer never arrives: the kernel's bounded wait ends (about
+    2 s), the result is NaN and the timeout is recorded; the context stays
+    usable. The "peer" is a second mailbox on this GPU that nothing writes."""
+    n = 4096
+    da, db, dc, dout = dev.put(np.ones(n, np.float32)), dev.put(np.ones(n, np.float32)), \
+        dev.alloc(4 * n), dev.alloc(8)
+    err, own = gpu.peer_mailbox_alloc()
+    err2, silent = gpu.peer_mailbox_alloc()
+    assert err == 0 and err2 == 0
+    try:
+        gpu.kernel_error(True)
+        assert gpu.vadd_sum_f32_allreduce(da.ptr, db.ptr, dc.ptr, n, dout.ptr, [own, silent], 0,
+                                          1) == 0
+        assert gpu.vcDeviceSynchronize() == 0
+        assert np.isnan(dout.to_host(np.float64, 1)[0])
+        assert gpu.kernel_error(True) != 0
+        # Still usable: a one-rank call right after succeeds.
+        assert gpu.vadd_sum_f32_allreduce(da.ptr, db.ptr, dc.ptr, n, dout.ptr, [own], 0, 2) == 0
+        assert gpu.vcDeviceSynchronize() == 0
+        assert float(dout.to_host(np.float64, 1)[0]) == 2.0 * n
+    finally:
+        gpu.peer_mailbox_free(own)
+        gpu.peer_mailbox_free(silent)
+
+
+def test_allreduce_rejects_bad_arguments(gpu, dev):
+    d = dev.alloc(1024)
+    err, mb = gpu.peer_mailbox_alloc()
+    assert err == 0
+    try:
+        bad = gpu.VCError.InvalidValue
+        assert gpu.vadd_sum_f32_allreduce(d.ptr, d.ptr, d.ptr, 16, d.ptr, [mb], 0, 0) == bad
+        assert gpu.vadd_sum_f32_allreduce(d.ptr, d.ptr, d.ptr, 16, d.ptr, [mb], 1, 1) == bad
+        assert gpu.vadd_sum_f32_allreduce(d.ptr, d.ptr, d.ptr, 16, d.ptr, [mb] * 9, 0, 1) == bad
+        assert gpu.vadd_sum_f32_allreduce(d.ptr, d.ptr, d.ptr, 16, d.ptr, [mb, 0], 0, 1) == bad
+        assert gpu.peer_ipc_open(b"\0" * 10)[0] == bad
+    finally:
+        gpu.peer_mailbox_free(mb)

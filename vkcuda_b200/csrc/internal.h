@@ -12,12 +12,32 @@ namespace vcb {
 int stream_max_blocks();
 cudaError_t launch_vadd_f32(const float *a, const float *b, float *c, int64_t n,
                             cudaStream_t stream);
+// Cross-GPU sum of the ranks' fp64 results without a library collective:
+// every rank owns one mailbox in its device memory; each rank's kernel
+// stores its result into slot `epoch & 1` of every mailbox over NVLink
+// (peer stores into memory mapped with CUDA IPC), then the epoch as a flag,
+// then waits (bounded) for all ranks' flags in its own mailbox and adds the
+// results in rank order, so every rank ends with the same value. Two slots
+// suffice: a rank can be at most one epoch ahead of any other.
+constexpr int kMaxPeers = 8;
+struct PeerMailbox {
+  double partial[2][kMaxPeers];
+  unsigned long long flag[2][kMaxPeers];
+};
+struct PeerExchange {
+  PeerMailbox *mbox[kMaxPeers];  // rank i's mailbox, as addressed from this GPU
+  int rank, world;               // world == 0: no exchange
+  unsigned long long epoch;      // >= 1, increasing per call
+};
+
 // Sum of x (or of c = x + b written out when b != nullptr) into *out (device
 // double). `partials` holds >= max_blocks doubles and `ticket` one zeroed
-// unsigned int; both are left ready for the next call.
+// unsigned int; both are left ready for the next call. With `px`, *out is the
+// sum over the ranks of `px` (see PeerExchange).
 cudaError_t launch_sum_f32(const float *x, const float *b, float *c, int64_t n,
                            double *out, double *partials, unsigned int *ticket,
-                           int max_blocks, cudaStream_t stream);
+                           int max_blocks, cudaStream_t stream,
+                           const PeerExchange *px = nullptr);
 cudaError_t launch_block_reduce_demo(const float *in, float *out, int n, int block,
                                      int groups, cudaStream_t stream);
 

@@ -1699,6 +1699,74 @@ int vc_vadd_sum_f32(const float *a, const float *b, float *c, int64_t n, double 
   use_current_device();
   return E(sum_common(a, b, c, n, out, reinterpret_cast<cudaStream_t>(s), "vc_vadd_sum_f32"));
 }
+int vc_peer_mailbox_alloc(void **mailbox) {
+  if (!mailbox) return E(VCError::InvalidValue);
+  if (!ensure_init()) return E(VCError::InitializationError);
+  use_current_device();
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, sizeof(vcb::PeerMailbox));
+  if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(vcb::PeerMailbox));
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return E(map_cuda(e, "vc_peer_mailbox_alloc"));
+  }
+  *mailbox = p;
+  return VC_SUCCESS;
+}
+int vc_peer_mailbox_free(void *mailbox) {
+  if (!mailbox) return VC_SUCCESS;
+  if (!ensure_init()) return E(VCError::InitializationError);
+  return E(map_cuda(cudaFree(mailbox), "vc_peer_mailbox_free"));
+}
+int vc_peer_ipc_get_handle(const void *dev_ptr, void *handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == VC_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!dev_ptr || !handle) return E(VCError::InvalidValue);
+  if (!ensure_init()) return E(VCError::InitializationError);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr));
+  if (e != cudaSuccess) return E(map_cuda(e, "vc_peer_ipc_get_handle"));
+  std::memcpy(handle, &h, sizeof(h));
+  return VC_SUCCESS;
+}
+int vc_peer_ipc_open(const void *handle, void **dev_ptr) {
+  if (!handle || !dev_ptr) return E(VCError::InvalidValue);
+  if (!ensure_init()) return E(VCError::InitializationError);
+  use_current_device();
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return E(map_cuda(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                    "vc_peer_ipc_open"));
+}
+int vc_peer_ipc_close(void *dev_ptr) {
+  if (!dev_ptr) return E(VCError::InvalidValue);
+  if (!ensure_init()) return E(VCError::InitializationError);
+  return E(map_cuda(cudaIpcCloseMemHandle(dev_ptr), "vc_peer_ipc_close"));
+}
+int vc_vadd_sum_f32_allreduce(const float *a, const float *b, float *c, int64_t n, double *out,
+                              void *const *mailboxes, int rank, int world,
+                              unsigned long long epoch, void *s) {
+  if (!a || !b || !c || !out || n < 0 || !mailboxes || world < 1 ||
+      world > vcb::kMaxPeers || rank < 0 || rank >= world || epoch == 0)
+    return E(VCError::InvalidValue);
+  vcb::PeerExchange px{};
+  for (int i = 0; i < world; ++i) {
+    if (!mailboxes[i]) return E(VCError::InvalidValue);
+    px.mbox[i] = static_cast<vcb::PeerMailbox *>(mailboxes[i]);
+  }
+  px.rank = rank;
+  px.world = world;
+  px.epoch = epoch;
+  if (!ensure_init()) return E(VCError::InitializationError);
+  use_current_device();
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
+  double *partials;
+  unsigned int *ticket;
+  int cap;
+  cudaError_t e = vcb::reduce_scratch(st, &partials, &ticket, &cap);
+  if (e != cudaSuccess) return E(run(e, "vc_vadd_sum_f32_allreduce"));
+  return E(run(vcb::launch_sum_f32(a, b, c, n, out, partials, ticket, cap, st, &px),
+               "vc_vadd_sum_f32_allreduce"));
+}
 int vc_block_reduce_f32(const float *in, float *out, int n, int block, int groups, void *s) {
   if (!in || !out || n < 0 || block <= 0 || block > 1024 || groups <= 0) return E(VCError::InvalidValue);
   if (!ensure_init()) return E(VCError::InitializationError);

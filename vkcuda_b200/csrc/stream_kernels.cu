@@ -86,11 +86,45 @@ __device__ __forceinline__ double block_sum_f64(double v, double *red) {
   return t;
 }
 
-// Last-block-done combine: block partials -> *out in index order; the ticket
-// counter is reset so the scratch is ready for the next launch.
+// Peer exchange of this GPU's total (one thread): store it into slot
+// epoch & 1 of every rank's mailbox, then the epoch as this rank's flag there
+// (a system-scope fence between, so a peer that sees the flag sees the
+// value), then wait for every rank's flag in this GPU's own mailbox and add
+// the values in rank order. A wait past kExchangeLimitNs records a timeout in
+// the device error word and gives NaN.
+constexpr unsigned long long kExchangeLimitNs = 2000000000ull;
+__device__ double exchange_sum(double total, const PeerExchange &px) {
+  const int slot = static_cast<int>(px.epoch & 1ull);
+  for (int i = 0; i < px.world; ++i)
+    *reinterpret_cast<volatile double *>(&px.mbox[i]->partial[slot][px.rank]) = total;
+  __threadfence_system();
+  for (int i = 0; i < px.world; ++i)
+    *reinterpret_cast<volatile unsigned long long *>(&px.mbox[i]->flag[slot][px.rank]) =
+        px.epoch;
+  PeerMailbox *own = px.mbox[px.rank];
+  const uint64_t t0 = global_timer_ns();
+  for (int i = 0; i < px.world; ++i) {
+    const volatile unsigned long long *f = &own->flag[slot][i];
+    for (uint32_t spin = 1; *f != px.epoch; ++spin) {
+      if ((spin & 255u) == 0u && global_timer_ns() - t0 > kExchangeLimitNs) {
+        record_error(kErrWaitTimeout);
+        return __longlong_as_double(0x7ff8000000000000ll);  // NaN
+      }
+    }
+  }
+  __threadfence_system();
+  double sum = 0.0;
+  for (int i = 0; i < px.world; ++i)
+    sum += *reinterpret_cast<const volatile double *>(&own->partial[slot][i]);
+  return sum;
+}
+
+// Last-block-done combine: block partials -> *out in index order (then, with
+// px.world > 0, summed over the ranks); the ticket counter is reset so the
+// scratch is ready for the next launch.
 __device__ __forceinline__ void combine_partials(double block_total, double *partials,
                                                  unsigned int *ticket, double *out,
-                                                 double *red) {
+                                                 double *red, const PeerExchange &px) {
   __shared__ bool is_last;
   if (threadIdx.x == 0) {
     partials[blockIdx.x] = block_total;
@@ -109,8 +143,8 @@ __device__ __forceinline__ void combine_partials(double block_total, double *par
   __syncthreads();
   const double total = block_sum_f64(v, red);
   if (threadIdx.x == 0) {
-    *out = total;
     *ticket = 0u;
+    *out = px.world > 0 ? exchange_sum(total, px) : total;
   }
 }
 
@@ -122,7 +156,7 @@ sum_vec_kernel(const float4 *__restrict__ x, const float4 *__restrict__ b,
                float4 *__restrict__ c, int64_t n4, const float *__restrict__ xs,
                const float *__restrict__ bs, float *__restrict__ cs,
                int64_t n, double *partials, unsigned int *ticket,
-               double *out) {
+               double *out, const PeerExchange px) {
   __shared__ double red[kStreamThreads / 32];
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -162,7 +196,7 @@ sum_vec_kernel(const float4 *__restrict__ x, const float4 *__restrict__ b,
   }
   const double total = block_sum_f64(acc, red);
   __syncthreads();
-  combine_partials(total, partials, ticket, out, red);
+  combine_partials(total, partials, ticket, out, red, px);
 }
 
 // Scalar-pointer form of sum for inputs that are not 16-byte aligned.
@@ -170,7 +204,7 @@ template <bool kFused>
 __global__ void __launch_bounds__(kStreamThreads)
 sum_scalar_kernel(const float *__restrict__ x, const float *__restrict__ b,
                   float *__restrict__ c, int64_t n, double *partials,
-                  unsigned int *ticket, double *out) {
+                  unsigned int *ticket, double *out, const PeerExchange px) {
   __shared__ double red[kStreamThreads / 32];
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   double acc = 0.0;
@@ -185,7 +219,7 @@ sum_scalar_kernel(const float *__restrict__ x, const float *__restrict__ b,
   }
   const double total = block_sum_f64(acc, red);
   __syncthreads();
-  combine_partials(total, partials, ticket, out, red);
+  combine_partials(total, partials, ticket, out, red, px);
 }
 
 // Demo block reduce. The pairing follows the reference tree exactly: with
@@ -272,8 +306,17 @@ cudaError_t launch_vadd_f32(const float *a, const float *b, float *c, int64_t n,
 
 cudaError_t launch_sum_f32(const float *x, const float *b, float *c, int64_t n,
                            double *out, double *partials, unsigned int *ticket,
-                           int max_blocks, cudaStream_t stream) {
+                           int max_blocks, cudaStream_t stream, const PeerExchange *pxp) {
   if (n < 0) return cudaErrorInvalidValue;
+  PeerExchange px{};
+  if (pxp != nullptr) {
+    if (pxp->world < 1 || pxp->world > kMaxPeers || pxp->rank < 0 || pxp->rank >= pxp->world ||
+        pxp->epoch == 0)
+      return cudaErrorInvalidValue;
+    for (int i = 0; i < pxp->world; ++i)
+      if (pxp->mbox[i] == nullptr) return cudaErrorInvalidValue;
+    px = *pxp;
+  }
   const bool fused = (b != nullptr);
   const bool vec = aligned16(x) && (!fused || (aligned16(b) && aligned16(c)));
   const int64_t units = vec ? (n / 4) / kUnroll + 1 : n / kUnroll + 1;
@@ -284,18 +327,18 @@ cudaError_t launch_sum_f32(const float *x, const float *b, float *c, int64_t n,
     if (fused)
       sum_vec_kernel<true><<<grid, kStreamThreads, 0, stream>>>(
           reinterpret_cast<const float4 *>(x), reinterpret_cast<const float4 *>(b),
-          reinterpret_cast<float4 *>(c), n4, x, b, c, n, partials, ticket, out);
+          reinterpret_cast<float4 *>(c), n4, x, b, c, n, partials, ticket, out, px);
     else
       sum_vec_kernel<false><<<grid, kStreamThreads, 0, stream>>>(
           reinterpret_cast<const float4 *>(x), nullptr, nullptr, n4, x, nullptr,
-          nullptr, n, partials, ticket, out);
+          nullptr, n, partials, ticket, out, px);
   } else {
     if (fused)
       sum_scalar_kernel<true><<<grid, kStreamThreads, 0, stream>>>(x, b, c, n, partials,
-                                                                   ticket, out);
+                                                                   ticket, out, px);
     else
       sum_scalar_kernel<false><<<grid, kStreamThreads, 0, stream>>>(
-          x, nullptr, nullptr, n, partials, ticket, out);
+          x, nullptr, nullptr, n, partials, ticket, out, px);
   }
   return cudaGetLastError();
 }

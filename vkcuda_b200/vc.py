@@ -141,6 +141,13 @@ SIGNATURES = {
     "vc_sum_f32": (_I, [_VP, _I64, _VP, _VP]),
     "vc_sum_f32_noalloc": (_I, [_VP, _I64, _VP, _VP]),
     "vc_vadd_sum_f32": (_I, [_VP, _VP, _VP, _I64, _VP, _VP]),
+    "vc_peer_mailbox_alloc": (_I, [ctypes.POINTER(ctypes.c_void_p)]),
+    "vc_peer_mailbox_free": (_I, [_VP]),
+    "vc_peer_ipc_get_handle": (_I, [_VP, _VP]),
+    "vc_peer_ipc_open": (_I, [_VP, ctypes.POINTER(ctypes.c_void_p)]),
+    "vc_peer_ipc_close": (_I, [_VP]),
+    "vc_vadd_sum_f32_allreduce": (_I, [_VP, _VP, _VP, _I64, _VP, ctypes.POINTER(ctypes.c_void_p),
+                                       _I, _I, ctypes.c_ulonglong, _VP]),
     "vc_block_reduce_f32": (_I, [_VP, _VP, _I, _I, _I, _VP]),
     "vc_gemm": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I64, _I64, _I64, _I64, _I, _I, _VP]),
     "vc_flash_fwd": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _F, _I, _I, _VP]),
@@ -490,6 +497,51 @@ def sum_f32_noalloc(x, n: int, out, stream=None) -> VCError:
 def vadd_sum_f32(a, b, c, n: int, out, stream=None) -> VCError:
     return VCError(library().vc_vadd_sum_f32(_addr(a), _addr(b), _addr(c), n, _addr(out),
                                              _stream(stream)))
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def peer_mailbox_alloc() -> Tuple[VCError, int]:
+    """One cross-GPU exchange mailbox in the current device's memory."""
+    p = ctypes.c_void_p(0)
+    e = VCError(library().vc_peer_mailbox_alloc(ctypes.byref(p)))
+    return e, (p.value or 0)
+
+
+def peer_mailbox_free(mailbox: int) -> VCError:
+    return VCError(library().vc_peer_mailbox_free(_addr(mailbox)))
+
+
+def peer_ipc_get_handle(dev_ptr: int) -> Tuple[VCError, bytes]:
+    """CUDA IPC handle (IPC_HANDLE_BYTES bytes) of a device allocation."""
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    e = VCError(library().vc_peer_ipc_get_handle(_addr(dev_ptr), buf))
+    return e, buf.raw
+
+
+def peer_ipc_open(handle: bytes) -> Tuple[VCError, int]:
+    """Map another process's allocation (from its handle) into this one."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        return VCError.InvalidValue, 0
+    buf = ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    p = ctypes.c_void_p(0)
+    e = VCError(library().vc_peer_ipc_open(buf, ctypes.byref(p)))
+    return e, (p.value or 0)
+
+
+def peer_ipc_close(dev_ptr: int) -> VCError:
+    return VCError(library().vc_peer_ipc_close(_addr(dev_ptr)))
+
+
+def vadd_sum_f32_allreduce(a, b, c, n: int, out, mailboxes, rank: int, epoch: int,
+                           stream=None) -> VCError:
+    """c = a + b; *out = sum over all ranks of sum(c), exchanged through the
+    ranks' mailboxes (all of them, in rank order) inside the kernel."""
+    arr = (ctypes.c_void_p * len(mailboxes))(*[_addr(m) for m in mailboxes])
+    return VCError(library().vc_vadd_sum_f32_allreduce(
+        _addr(a), _addr(b), _addr(c), n, _addr(out), arr, rank, len(mailboxes), epoch,
+        _stream(stream)))
 
 
 def block_reduce_f32(inp, out, n: int, block: int, groups: int, stream=None) -> VCError:
