@@ -432,22 +432,8 @@ def stream_workload(vc, dist, steps, warmup, pk):
     # N > 1: the per-GPU sums are combined inside the kernel through the
     # ranks' mailboxes (NVLink peer stores); the handles travel once over the
     # process group.
-    boxes = None
-    if dist.pg:
-        err, own = vc.peer_mailbox_alloc()
-        check(err, "vc_peer_mailbox_alloc")
-        err, handle = vc.peer_ipc_get_handle(own)
-        check(err, "vc_peer_ipc_get_handle")
-        handles = [None] * dist.world
-        dist.pg.all_gather_object(handles, handle)
-        boxes = []
-        for i, h in enumerate(handles):
-            if i == dist.rank:
-                boxes.append(own)
-            else:
-                err, ptr = vc.peer_ipc_open(h)
-                check(err, "vc_peer_ipc_open")
-                boxes.append(ptr)
+    from vkcuda_b200 import peer
+    boxes = peer.open_mailboxes(dist.pg, dist.rank, dist.world) if dist.pg else None
     epoch = [0]
 
     def fused():
@@ -489,12 +475,7 @@ def stream_workload(vc, dist, steps, warmup, pk):
     ms_ar = timed(dist, stream, lambda: dist.pg.all_reduce(part), steps, warmup) if dist.pg else None
     if boxes is not None:
         torch.cuda.synchronize()
-        dist.barrier()  # no rank stores into a mailbox after this
-        for i, ptr in enumerate(boxes):
-            if i != dist.rank:
-                check(vc.peer_ipc_close(ptr), "vc_peer_ipc_close")
-        dist.barrier()
-        check(vc.peer_mailbox_free(boxes[dist.rank]), "vc_peer_mailbox_free")
+        peer.close_mailboxes(dist.pg, dist.rank, boxes)
     per = ms_fused / steps
     gbs = 12.0 * n_total / (per * 1e-3) / 1e9
     local_gbs = 12.0 * n / (per * 1e-3) / 1e9

@@ -18,20 +18,8 @@ def main() -> int:
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     torch.cuda.set_device(rank)
     assert vc.vcInit() == 0 and vc.vcSetDevice(rank) == 0
-    err, own = vc.peer_mailbox_alloc()
-    assert err == 0
-    err, handle = vc.peer_ipc_get_handle(own)
-    assert err == 0
-    handles = [None] * world
-    dist.all_gather_object(handles, handle)
-    boxes = []
-    for i, h in enumerate(handles):
-        if i == rank:
-            boxes.append(own)
-        else:
-            err, p = vc.peer_ipc_open(h)
-            assert err == 0, err
-            boxes.append(p)
+    from vkcuda_b200 import peer
+    boxes = peer.open_mailboxes(dist, rank, world)
     n = (1 << 22) + 17 * rank + 3
     g = torch.Generator(device="cuda").manual_seed(100 + rank)
     a = torch.rand(n, device="cuda", generator=g)
@@ -53,12 +41,7 @@ def main() -> int:
         dist.all_gather(gots, torch.tensor([got], dtype=torch.float64))
         assert all(t.item() == got for t in gots), "ranks disagree"
     assert vc.kernel_error(True) == 0
-    dist.barrier()  # nobody writes into a mailbox after this point
-    for i, p in enumerate(boxes):
-        if i != rank:
-            assert vc.peer_ipc_close(p) == 0
-    dist.barrier()
-    assert vc.peer_mailbox_free(own) == 0
+    peer.close_mailboxes(dist, rank, boxes)
     dist.destroy_process_group()
     print(f"rank {rank} ok", flush=True)
     return 0

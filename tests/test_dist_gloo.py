@@ -1,8 +1,10 @@
 """Multi-process host logic of the sharded paths, on CPU with world size 2
 over gloo: contiguous shards cover every unit exactly once, per-rank fp64
-partials combined by one all-reduce equal the whole sum (the streaming pair's
-exchange step), and a rank that fails before a collective is detected by the
-other rank as an error within the process-group timeout instead of a hang."""
+partials combined across ranks equal the whole sum, the mailbox exchange of
+the in-kernel cross-GPU sum hands every rank all mailboxes in rank order
+(vkcuda_b200.peer with fake device calls), and a rank that fails before a
+collective is detected by the other rank as an error within the
+process-group timeout instead of a hang."""
 from __future__ import annotations
 
 import os
@@ -41,6 +43,34 @@ def _worker(rank, world, port, mode, q):
             part = torch.tensor([oracle.sum_f64(x[b0:b1])], dtype=torch.float64)
             dist.all_reduce(part)
             q.put((rank, "sum", float(part.item()), oracle.sum_f64(x), (b0, b1)))
+        elif mode == "mailboxes":
+            # vkcuda_b200.peer's exchange with fake device calls: addresses
+            # encode their owner, so the result shows who mapped what.
+            from vkcuda_b200 import peer
+            log = {"opened": [], "closed": [], "freed": []}
+            own = 0x1000 + rank
+
+            def alloc():
+                return 0, own
+
+            def get_handle(ptr):
+                return 0, bytes([ptr & 0xff]) * 64
+
+            def open_handle(h):
+                log["opened"].append(h[0])
+                return 0, 0x9000 + h[0]
+
+            def close_handle(ptr):
+                log["closed"].append(ptr)
+                return 0
+
+            def free(ptr):
+                log["freed"].append(ptr)
+                return 0
+
+            boxes = peer.open_mailboxes(dist, rank, world, alloc, get_handle, open_handle)
+            peer.close_mailboxes(dist, rank, boxes, close_handle, free)
+            q.put((rank, "mailboxes", boxes, log))
         elif mode == "fail":
             if rank == 1:
                 raise RuntimeError("rank 1 fails before the collective")
@@ -102,3 +132,20 @@ def test_rank_failure_detected_not_hung():
     by_rank = {r[0]: r[1:] for r in res}
     assert by_rank[1][0] == "raised"
     assert by_rank[0][0] == "detected"
+
+
+def test_peer_mailbox_exchange_world2():
+    """Host side of the in-kernel cross-GPU sum: every rank ends with all
+    mailbox addresses in rank order (its own allocation at its rank, the
+    others mapped from their handles), and unmaps exactly the others' and
+    frees only its own."""
+    res = _run("mailboxes")
+    assert len(res) == 2
+    for rank, kind, boxes, log in res:
+        assert kind == "mailboxes"
+        other = 1 - rank
+        assert boxes[rank] == 0x1000 + rank
+        assert boxes[other] == 0x9000 + other  # mapped from the other rank's handle
+        assert log["opened"] == [other]
+        assert log["closed"] == [boxes[other]]
+        assert log["freed"] == [0x1000 + rank]
