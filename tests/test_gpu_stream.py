@@ -192,3 +192,34 @@ def test_allreduce_rejects_bad_arguments(gpu, dev):
         assert gpu.peer_ipc_open(b"\0" * 10)[0] == bad
     finally:
         gpu.peer_mailbox_free(mb)
+
+
+def test_vadd_sum_full_size_2p30(gpu):
+    """The benchmark size, 2^30 fp32 elements (12 GiB of operands): c = a + b
+    bit-identical to torch's IEEE add, the sum within 1e-6 of an fp64
+    reduction, also through the one-rank exchange path."""
+    import torch
+    n = 1 << 30
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.rand(n, device="cuda", generator=g)
+    b = torch.rand(n, device="cuda", generator=g)
+    c = torch.empty_like(a)
+    out = torch.zeros(1, dtype=torch.float64, device="cuda")
+    assert gpu.vadd_sum_f32(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, out.data_ptr()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(c, a + b)
+    ref = c.double().sum().item()
+    assert abs(out.item() - ref) <= SUM_RTOL * abs(ref)
+    err, mb = gpu.peer_mailbox_alloc()
+    assert err == 0
+    try:
+        out.zero_()
+        assert gpu.vadd_sum_f32_allreduce(a.data_ptr(), b.data_ptr(), c.data_ptr(), n,
+                                          out.data_ptr(), [mb], 0, 1) == 0
+        torch.cuda.synchronize()
+        assert abs(out.item() - ref) <= SUM_RTOL * abs(ref)
+    finally:
+        gpu.peer_mailbox_free(mb)
+    assert gpu.kernel_error(True) == 0
+    del a, b, c
+    torch.cuda.empty_cache()
