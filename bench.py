@@ -70,6 +70,18 @@ def traffic_table():
     return {}
 
 
+def flash_traffic(name, bh):
+    """DRAM bytes of one launch over `bh` slices: a whole-launch capture of
+    this workload when there is one, else a per-slice figure (a capture of
+    fewer slices of the same shape, whose traffic grows with the slice
+    count) times `bh`."""
+    tt = traffic_table()
+    if name in tt:
+        return tt[name]
+    per_slice = tt.get(name + "_per_slice")
+    return None if per_slice is None else int(per_slice * bh)
+
+
 class ClockSampler:
     """nvidia-smi samples (every 50 ms) while the timed region runs."""
 
@@ -408,7 +420,7 @@ def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk,
                         "peak_kind": ("bf16 dense sustained" if long_kernel else "bf16 dense burst")
                         + f" ({pk['source']}); timed region {ms / 1e3:.2f} s",
                         "frac_vs_burst": round(achieved / pk["bf16"], 4),
-                        "traffic": traffic_table().get(name)},
+                        "traffic": flash_traffic(name, bh)},
            "gpu_launches": steps, "parity_guard_max_err": perr}
     if dtype == vc.Dtype.F32:
         res["roofline"]["note"] = "fp32 CUDA-core path; latency bound at this size"
@@ -537,6 +549,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--only", default="gemm,fa_causal,fa_bf16,stream,fa_f32")
+    ap.add_argument("--fa-bf16-heads", type=int, default=32,
+                    help="heads of the bf16 attention config (32); a smaller count gives a "
+                         "launch small enough for an ncu capture, whose DRAM traffic scales "
+                         "with batch x heads")
     ap.add_argument("--gemms-per-step", type=int, default=GEMMS_PER_STEP,
                     help="GEMM products per step (small values for profiler captures)")
     args = ap.parse_args()
@@ -580,7 +596,8 @@ def main():
     jobs = [("fa_causal", lambda: flash_workload(vc, dist, "fa_causal", 8, 16, 4096, 128, True,
                                                  vc.Dtype.F16, max(args.steps, 20), args.warmup, pk,
                                                  shard_bh=False)),
-            ("fa_bf16", lambda: flash_workload(vc, dist, "fa_bf16", 32, 32, 8192, 128, False,
+            ("fa_bf16", lambda: flash_workload(vc, dist, "fa_bf16", 32, args.fa_bf16_heads, 8192, 128,
+                                               False,
                                                vc.Dtype.BF16, max(3, min(args.steps, 5)),
                                                args.warmup, pk, shard_bh=True)),
             ("stream", lambda: stream_workload(vc, dist, max(args.steps, 10), args.warmup, pk)),
