@@ -82,6 +82,14 @@ def flash_traffic(name, bh):
     return None if per_slice is None else int(per_slice * bh)
 
 
+def stream_traffic(n):
+    """DRAM bytes of one fused vadd+sum launch over `n` elements: a capture
+    of the same kernel on fewer elements (inputs still larger than L2), per
+    element, times `n`."""
+    per_elem = traffic_table().get("stream_fused_per_elem")
+    return None if per_elem is None else int(per_elem * n)
+
+
 class ClockSampler:
     """nvidia-smi samples (every 50 ms) while the timed region runs."""
 
@@ -429,9 +437,9 @@ def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk,
     return res
 
 
-def stream_workload(vc, dist, steps, warmup, pk):
+def stream_workload(vc, dist, steps, warmup, pk, log2n=30):
     import torch
-    n_total = 1 << 30
+    n_total = 1 << log2n
     b0, b1 = shard(n_total, dist.world, dist.rank)
     n = b1 - b0
     g = torch.Generator(device="cuda").manual_seed(5 + dist.rank)
@@ -501,7 +509,7 @@ def stream_workload(vc, dist, steps, warmup, pk):
                               "combined inside the kernel through NVLink peer stores"},
            "roofline": {"bound": "hbm", "achieved": round(local_gbs, 1), "peak": pk["hbm"],
                         "unit": "GB/s", "frac": round(local_gbs / pk["hbm"], 4),
-                        "bytes_per_elem": 12, "traffic": traffic_table().get("stream_fused")},
+                        "bytes_per_elem": 12, "traffic": stream_traffic(n)},
            "separate_kernels": {"vadd_gbs": round(vadd_gbs, 1), "sum_gbs": round(sum_gbs, 1),
                                 "pair_gbs_16B": round(pair_gbs, 1),
                                 "vadd_frac": round(vadd_gbs / pk["hbm"], 4),
@@ -553,6 +561,10 @@ def main():
                     help="heads of the bf16 attention config (32); a smaller count gives a "
                          "launch small enough for an ncu capture, whose DRAM traffic scales "
                          "with batch x heads")
+    ap.add_argument("--stream-log2n", type=int, default=30,
+                    help="log2 of the streaming pair's element count (30); a smaller size "
+                         "gives a launch small enough for an ncu capture, whose DRAM traffic "
+                         "scales with the element count")
     ap.add_argument("--gemms-per-step", type=int, default=GEMMS_PER_STEP,
                     help="GEMM products per step (small values for profiler captures)")
     args = ap.parse_args()
@@ -600,7 +612,8 @@ def main():
                                                False,
                                                vc.Dtype.BF16, max(3, min(args.steps, 5)),
                                                args.warmup, pk, shard_bh=True)),
-            ("stream", lambda: stream_workload(vc, dist, max(args.steps, 10), args.warmup, pk)),
+            ("stream", lambda: stream_workload(vc, dist, max(args.steps, 10), args.warmup, pk,
+                                               args.stream_log2n)),
             ("fa_f32", lambda: flash_workload(vc, dist, "fa_f32", 1, 1, 256, 64, False,
                                               vc.Dtype.F32, max(args.steps, 20), args.warmup, pk,
                                               shard_bh=False))]
