@@ -30,6 +30,7 @@ SOURCES = [
     "runtime.cpp",
     "stream_kernels.cu",
     "gemm_tcgen05.cu",
+    "gemm_f32_tcgen05.cu",
     "gemm_simt.cu",
     "flash_fwd_tcgen05.cu",
     "flash_fwd_f32.cu",

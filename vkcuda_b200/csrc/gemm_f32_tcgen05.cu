@@ -1,0 +1,472 @@
+// gemm_f32_tcgen05.cu - fp32 D[M][N] = A[M][K] * B (+ Cin) on sm_100a tensor
+// cores with fp32-level accuracy.
+//
+// Replaces the reference's fp32 SIMT GEMM, matmulTiled
+// (examples/matmul_bench.vc:22-54: one thread per output, 16x16 tiles of A
+// and B through shared memory, fp32 multiply-add over K), whose bar is 1e-4
+// relative error against an fp64 loop (matmul_bench.vc:109-125).
+//
+// Method (the three-term tf32 split product, "3xTF32"): every fp32 operand x
+// is split into hi = x with its low 13 mantissa bits cleared (exactly a tf32
+// value) and lo = x - hi (exact in fp32, |lo| < 2^-10 |x|); the tensor cores
+// accumulate lo_a*hi_b + hi_a*lo_b + hi_a*hi_b in fp32 with tcgen05.mma
+// kind::tf32. The MMA reads lo to tf32 precision, and the dropped lo_a*lo_b
+// term is below 2^-20 |a*b|, so each product carries ~2^-19 relative error
+// against ~2^-24 for an fp32 FMA: far inside 1e-4 at any K the demos use.
+// Non-finite x keeps hi = x, lo = 0; an infinity then meets the other
+// operand's lo (usually 0) and its outputs read NaN where fp32 FMA gives inf.
+//
+// Design: CTA pairs (cluster of two, cta_group::2), 256 x 256 output tiles,
+// one persistent cluster per SM pair, 320 threads per CTA:
+//   warp 0      TMA producer (each CTA): per 32-deep K stage, this CTA's 128
+//               rows of A (128 x 32 fp32 = 16 KiB) and its 128-column half of
+//               the B panel (16 KiB), 128-byte swizzled, 3-stage ring.
+//   warps 6..9  split (each CTA): once a stage lands, rewrite it in place as
+//               hi and write lo beside it (same swizzled layout), fence the
+//               writes to the tensor proxy, arrive on CTA 0's split barrier.
+//   warp 1      CTA 0 lane 0 issues 3 pair MMAs (M = 256, N = 256, K = 8)
+//               per 8-deep K step from both CTAs' shared memory into TMEM
+//               (2 x 256-column accumulators, one per 256-deep K chunk,
+//               alternating); its commits free the stage in both CTAs and
+//               hand each chunk to the epilogues.
+//   warps 2..5  epilogue (each CTA): tcgen05.ld of its 128 accumulator rows,
+//               32 x 32 swizzled boxes TMA-stored for the first K chunk (with
+//               the optional Cin addend) and TMA reduce-added for the rest.
+// B stored [K][N] (the demos' layout) is an MN-major operand; for tf32 that
+// takes the 128-byte swizzle with 32-byte atoms, in TMA and descriptor.
+// Shared memory per stage: A raw/hi, B raw/hi, A lo, B lo = 64 KiB; 3 stages
+// + 32 KiB of epilogue staging = 224 KiB. Ragged M, N, K: TMA zero-fills
+// loads outside the matrix (zero splits into zero hi and lo) and clips
+// stores. Roofline: 3 x 2*M*N*K tf32 FLOP on the tensor pipe, whose dense
+// rate is half the fp16 rate; 2*M*N*K fp32 FLOP delivered.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <mutex>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace vcb {
+namespace {
+
+constexpr int BM = 128;               // rows of A per CTA (256 per pair)
+constexpr int BN = 256;               // output columns per pair tile
+constexpr int BK = 32;                // 32 fp32 = one 128-byte swizzle row
+constexpr int kStages = 3;
+constexpr uint32_t kTileBytes = 128 * BK * 4;         // 16 KiB
+constexpr uint32_t kRawBytes = 2 * kTileBytes;        // A, B as loaded
+constexpr uint32_t kStageBytes = 2 * kRawBytes;       // + A lo, B lo
+constexpr int kAccCols = BN;
+constexpr uint32_t kTmemCols = 2 * kAccCols;
+constexpr int kEpiCols = 32;
+constexpr uint32_t kEpiBytes = BM * kEpiCols * 4;
+constexpr int kThreads = 320;
+constexpr int kEpiThreads = 128;
+constexpr int kSplitWarps = 4;
+constexpr int kSplitThreads = kSplitWarps * 32;
+constexpr int kSplitChunks = kRawBytes / 16 / kSplitThreads;  // 16-byte chunks per thread
+constexpr int kGroupRows = 8;
+constexpr size_t kGroupAboveBBytes = 64ull << 20;
+// The tensor cores' fp32 accumulation truncates: a running sum loses about
+// 2^-24.5 of itself per MMA (measured: 6.5e-6 relative after K = 256 of
+// same-sign data, growing with K). So each tile accumulates K in chunks of
+// kChunkK in TMEM, and the epilogue adds the chunks into D with round-to-
+// nearest reduce-adds (TMA bulk reduce), bounding the truncation to one
+// chunk's worth.
+constexpr int kChunkK = 256;
+
+struct __align__(8) F32Barriers {
+  uint64_t full[kStages];    // each CTA: its own TMA bytes landed
+  uint64_t split[kStages];   // CTA 0: both CTAs' split warps done
+  uint64_t empty[kStages];   // each CTA: the MMAs reading the stage completed
+  uint64_t acc_full[2];      // each CTA
+  uint64_t acc_empty[2];     // CTA 0 (both epilogues arrive)
+  uint32_t tmem_base;
+};
+
+constexpr size_t kSmemBytes =
+    1024 + kStages * kStageBytes + 2 * kEpiBytes + sizeof(F32Barriers);
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kRawBytes % (16 * kSplitThreads) == 0, "split work divides evenly");
+
+// hi: x with the low 13 mantissa bits cleared; lo = x - hi (exact).
+__device__ __forceinline__ void split_tf32(uint32_t x, uint32_t &hi, uint32_t &lo) {
+  const bool finite = (x & 0x7f800000u) != 0x7f800000u;
+  hi = finite ? (x & 0xffffe000u) : x;
+  lo = finite ? __float_as_uint(__uint_as_float(x) - __uint_as_float(hi)) : 0u;
+}
+
+// Stage this warp's 32 x 32 box (128-byte swizzle, as the D map) and store
+// it, or add it onto D (round to nearest) when `add` is set.
+__device__ __forceinline__ void epilogue_store_box(const CUtensorMap *tmD, uint8_t *warp_stage,
+                                                   uint32_t (&v)[32], int lane, uint32_t &count,
+                                                   int x, int y, bool add) {
+  const int buf = count & 1;
+  if (lane == 0) bulk_wait_group_read<1>();
+  __syncwarp();
+  uint8_t *dst = warp_stage + buf * 4096 + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<uint4 *>(dst + ((j ^ (lane & 7)) * 16)) =
+        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (add) tma_reduce_add_2d(tmD, warp_stage + buf * 4096, x, y);
+    else tma_store_2d(tmD, warp_stage + buf * 4096, x, y);
+    bulk_commit_group();
+  }
+  ++count;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmD,
+                     const float *__restrict__ Cin, int64_t ldc, int M, int N, int K,
+                     uint32_t idesc_full, uint32_t idesc_half, int b_kn, int num_full,
+                     int num_units, int group_rows, int chunk_kblocks) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *stage_base = smem;
+  uint8_t *epi_base = smem + kStages * kStageBytes;
+  F32Barriers *bars = reinterpret_cast<F32Barriers *>(epi_base + 2 * kEpiBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int tiles_m = (M + 2 * BM - 1) / (2 * BM);
+  const int kblocks = (K + BK - 1) / BK;
+  // Unit -> tile as in the fp16 pair kernel: full 256 x 256 tiles, then the
+  // tail wave's tiles as 256 x 128 halves; groups of `group_rows` pair rows
+  // walked column by column.
+  auto unit_tile = [&](int u, int &tm, int &n0, int &width) {
+    int tile = u, half = 0;
+    width = BN;
+    if (u >= num_full) {
+      tile = num_full + (u - num_full) / 2;
+      half = (u - num_full) & 1;
+      width = BN / 2;
+    }
+    const int group = tile / (group_rows * tiles_n);
+    const int first_m = group * group_rows;
+    const int rows = min(tiles_m - first_m, group_rows);
+    const int in_group = tile - group * group_rows * tiles_n;
+    tm = first_m + in_group % rows;
+    n0 = (in_group / rows) * BN + half * (BN / 2);
+  };
+  auto lead = [&](uint64_t *b) { return mapa_shared(smem_u32(b), 0); };
+  auto peer = [&](uint64_t *b) { return mapa_shared(smem_u32(b), 1); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->split[s], 2 * kSplitWarps);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 2 * kEpiThreads);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmD);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (each CTA, its own barriers)
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int u = cluster; ok && u < num_units; u += num_clusters) {
+        int tm, n0, width;
+        unit_tile(u, tm, n0, width);
+        const int a_row = tm * 2 * BM + rank * BM;
+        const int b_col = n0 + rank * (width / 2);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bars->empty[stage], phase ^ 1u)) { ok = false; break; }
+          uint8_t *sA = stage_base + stage * kStageBytes;
+          uint8_t *sB = sA + kTileBytes;
+          mbar_arrive_expect_tx(&bars->full[stage], kRawBytes);
+          tma_load_2d(sA, &tmA, kb * BK, a_row, &bars->full[stage]);
+          if (b_kn) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              tma_load_2d(sB + j * (32 * BK * 4), &tmB, b_col + j * 32, kb * BK,
+                          &bars->full[stage]);
+          } else {
+            tma_load_2d(sB, &tmB, kb * BK, b_col, &bars->full[stage]);
+          }
+          ++issued;
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: every issued copy lands before the CTA may exit.
+      const uint32_t last = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
+      for (uint32_t i = 0; i < last; ++i) {
+        const uint32_t idx = issued - 1 - i;
+        mbar_wait(&bars->full[idx % kStages], (idx / kStages) & 1u, 1000000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (CTA 0)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      // One accumulator per (unit, K chunk), alternating between the two.
+      for (int u = cluster; ok && u < num_units; u += num_clusters) {
+       for (int kb0 = 0; ok && kb0 < kblocks; kb0 += chunk_kblocks, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        const uint32_t idesc = (u < num_full) ? idesc_full : idesc_half;
+        if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kAccCols;
+        const int kb_end = min(kblocks, kb0 + chunk_kblocks);
+        for (int kb = kb0; kb < kb_end; ++kb) {
+          // Cluster-scope acquire: the other CTA's split writes (fenced to
+          // the tensor proxy before its release arrive) precede these MMAs.
+          if (!mbar_wait_cluster(&bars->split[stage], phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(stage_base + stage * kStageBytes);
+          const uint32_t b_hi = a_hi + kTileBytes;
+          const uint32_t a_lo = a_hi + kRawBytes;
+          const uint32_t b_lo = b_hi + kRawBytes;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            // K-major: 8 fp32 = 32 bytes per step inside the swizzle row.
+            // MN-major B (32-byte-atom swizzle): 8 K-rows = 1024 bytes per
+            // step, 4-row groups 512 bytes apart, 32-column blocks BK x 128
+            // bytes apart.
+            const uint64_t adh = smem_desc_sw128(a_hi + k * 32, 16, 1024);
+            const uint64_t adl = smem_desc_sw128(a_lo + k * 32, 16, 1024);
+            const uint64_t bdh = b_kn ? smem_desc_sw128_atom32(b_hi + k * 1024, BK * 128, 512)
+                                      : smem_desc_sw128(b_hi + k * 32, 16, 1024);
+            const uint64_t bdl = b_kn ? smem_desc_sw128_atom32(b_lo + k * 1024, BK * 128, 512)
+                                      : smem_desc_sw128(b_lo + k * 32, 16, 1024);
+            mma_tf32_ss_pair(d_tmem, adl, bdh, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            mma_tf32_ss_pair(d_tmem, adh, bdl, idesc, 1u);
+            mma_tf32_ss_pair(d_tmem, adh, bdh, idesc, 1u);
+          }
+          mma_commit_pair(lead(&bars->empty[stage]));
+          mma_commit_pair(peer(&bars->empty[stage]));
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit_pair(lead(&bars->acc_full[acc]));
+        mma_commit_pair(peer(&bars->acc_full[acc]));
+       }
+      }
+    }
+  } else if (warp >= 6) {
+    // ---------------- split warps (each CTA)
+    const int t = threadIdx.x - 6 * 32;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int u = cluster; ok && u < num_units; u += num_clusters) {
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->full[stage], phase))) { ok = false; break; }
+        uint8_t *raw = stage_base + stage * kStageBytes;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint4 v[kSplitChunks / 2];
+#pragma unroll
+          for (int i = 0; i < kSplitChunks / 2; ++i)
+            v[i] = *reinterpret_cast<const uint4 *>(
+                raw + ((half * (kSplitChunks / 2) + i) * kSplitThreads + t) * 16);
+#pragma unroll
+          for (int i = 0; i < kSplitChunks / 2; ++i) {
+            uint4 hi, lo;
+            split_tf32(v[i].x, hi.x, lo.x);
+            split_tf32(v[i].y, hi.y, lo.y);
+            split_tf32(v[i].z, hi.z, lo.z);
+            split_tf32(v[i].w, hi.w, lo.w);
+            const uint32_t off = ((half * (kSplitChunks / 2) + i) * kSplitThreads + t) * 16;
+            *reinterpret_cast<uint4 *>(raw + off) = hi;
+            *reinterpret_cast<uint4 *>(raw + kRawBytes + off) = lo;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(&bars->split[stage]);
+          else mbar_arrive_cluster(lead(&bars->split[stage]));
+        }
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else {
+    // ---------------- epilogue (each CTA): warps 2..5, thread = row
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    uint8_t *warp_stage = epi_base + quad * 8192;
+    const uint32_t acc_empty_lead0 = lead(&bars->acc_empty[0]);
+    const uint32_t acc_empty_lead1 = lead(&bars->acc_empty[1]);
+    int local = 0;
+    uint32_t box_count = 0;
+    bool ok = true;
+    for (int u = cluster; ok && u < num_units; u += num_clusters) {
+      int tm, n0, width;
+      unit_tile(u, tm, n0, width);
+      const int m0 = tm * 2 * BM + rank * BM;
+      const int gr = m0 + row;
+      const int nboxes = width / kEpiCols;
+      for (int kb0 = 0; kb0 < kblocks; kb0 += chunk_kblocks, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&bars->acc_full[acc], acc_phase)) { ok = false; break; }
+        tc_fence_after();
+        const bool first = kb0 == 0;
+        // A later K chunk adds onto what this warp stored for the earlier
+        // ones: those writes must have completed first.
+        if (!first) {
+          if (lane == 0) bulk_wait_group<0>();
+          __syncwarp();
+        }
+        for (int c = 0; c < nboxes; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * kAccCols + c * kEpiCols, v);
+          tmem_ld_wait();
+          if (c == nboxes - 1) {
+            tc_fence_before();
+            if (rank == 0) mbar_arrive(&bars->acc_empty[acc]);
+            else mbar_arrive_cluster(acc ? acc_empty_lead1 : acc_empty_lead0);
+          }
+          const int cn0 = n0 + c * kEpiCols;
+          if (cn0 >= N) continue;
+          if (first && Cin != nullptr && gr < M) {
+            const float *crow = Cin + (int64_t)gr * ldc;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (cn0 + j < N) v[j] = __float_as_uint(__uint_as_float(v[j]) + crow[cn0 + j]);
+          }
+          epilogue_store_box(&tmD, warp_stage, v, lane, box_count, cn0, m0 + quad * 32, !first);
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
+}
+
+struct F32MapCache {
+  GemmArgs key{};
+  int device = -1;
+  CUtensorMap a, b, d;
+  bool valid = false;
+};
+
+bool same_key(const GemmArgs &x, const GemmArgs &y) {
+  return x.A == y.A && x.B == y.B && x.D == y.D && x.M == y.M && x.N == y.N &&
+         x.K == y.K && x.lda == y.lda && x.ldb == y.ldb && x.ldd == y.ldd &&
+         x.b_kn == y.b_kn;
+}
+
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int clusters_resident(int dev, int sms) {
+  static int cached[64] = {0};
+  if (dev < 0 || dev >= 64) return sms / 2;
+  if (cached[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms & ~1, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_f32_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sms / 2;
+    }
+    cached[dev] = n < sms / 2 ? n : sms / 2;
+  }
+  return cached[dev];
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_f32_tcgen05(const GemmArgs &g, cudaStream_t stream) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return cudaErrorInvalidValue;
+  if (!al16(g.A) || !al16(g.B) || !al16(g.D)) return cudaErrorNotSupported;
+  if (g.lda % 4 || g.ldb % 4 || g.ldd % 4) return cudaErrorNotSupported;
+  if (g.lda < g.K || g.ldd < g.N) return cudaErrorInvalidValue;
+  if (g.b_kn ? g.ldb < g.N : g.ldb < g.K) return cudaErrorInvalidValue;
+  if (g.Cin && g.ldc < g.N) return cudaErrorInvalidValue;
+
+  static thread_local F32MapCache cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(cache.valid && cache.device == dev && same_key(cache.key, g))) {
+    const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    bool ok = make_map_2d(&cache.a, f32, 4, g.A, g.K, g.M, g.lda, BK, BM);
+    if (g.b_kn)
+      ok = ok && make_map_2d(&cache.b, f32, 4, g.B, g.N, g.K, g.ldb, 32, BK,
+                             CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    else
+      ok = ok && make_map_2d(&cache.b, f32, 4, g.B, g.K, g.N, g.ldb, BK, BN / 2);
+    ok = ok && make_map_2d(&cache.d, f32, 4, g.D, g.N, g.M, g.ldd, kEpiCols, 32);
+    if (!ok) {
+      cache.valid = false;
+      return cudaErrorNotSupported;
+    }
+    cache.key = g;
+    cache.device = dev;
+    cache.valid = true;
+  }
+
+  static uint64_t configured_device_mask = 0;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 64 || !(configured_device_mask & (1ull << dev))) {
+      cudaError_t e = cudaFuncSetAttribute(gemm_f32_pair_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kSmemBytes);
+      if (e != cudaSuccess) return e;
+      if (dev < 64) configured_device_mask |= (1ull << dev);
+    }
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms < 2) return cudaErrorNotSupported;
+  const int pair_tiles = ((g.M + 2 * BM - 1) / (2 * BM)) * ((g.N + BN - 1) / BN);
+  const int resident = clusters_resident(dev, sms);
+  const int clusters = pair_tiles < resident ? pair_tiles : resident;
+  const int tail = pair_tiles % clusters;
+  const bool split = tail > 0 && 2 * tail <= clusters;
+  const int num_full = split ? pair_tiles - tail : pair_tiles;
+  const int num_units = split ? num_full + 2 * tail : pair_tiles;
+  const uint32_t idesc_full = idesc_tf32_f32(2 * BM, BN, false, g.b_kn);
+  const uint32_t idesc_half = idesc_tf32_f32(2 * BM, BN / 2, false, g.b_kn);
+  gemm_f32_pair_kernel<<<2 * clusters, kThreads, kSmemBytes, stream>>>(
+      cache.a, cache.b, cache.d, g.Cin, g.ldc, g.M, g.N, g.K, idesc_full, idesc_half,
+      g.b_kn ? 1 : 0, num_full, num_units,
+      (size_t)g.K * (size_t)g.N * 4 > kGroupAboveBBytes ? kGroupRows : 1, kChunkK / BK);
+  return cudaGetLastError();
+}
+
+}  // namespace vcb
+
+VCB_DEFINE_ERROR_ACCESSOR(gemm_f32_error)

@@ -3,8 +3,10 @@
 //   * fp16/bf16 -> fp32 GEMM with arbitrary strides and alignment (row
 //     strides that break TMA's 16-byte rule), same contract as the tcgen05
 //     path: D = A * B (+ Cin), fp32 accumulation in K order;
-//   * fp32 C = A * B, the reference's SIMT benchmark kernel matmulTiled
-//     (examples/matmul_bench.vc:22-54), 16x16 shared-memory tiles.
+//   * fp32 D = A * B (+ Cin) with strides the fp32 tensor-core path
+//     (gemm_f32_tcgen05.cu) cannot take; that path serves the reference's
+//     SIMT benchmark kernel matmulTiled (examples/matmul_bench.vc:22-54,
+//     16x16 shared-memory tiles) otherwise.
 // Both use 64x64 output tiles per 256-thread block with 4x4 outputs per
 // thread and 16-deep K slabs staged in shared memory.
 #include <cuda_bf16.h>
@@ -104,13 +106,13 @@ cudaError_t launch_gemm_simt(const GemmArgs &g, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_matmul_f32(const float *A, const float *B, float *C, int M, int N,
-                              int K, int64_t lda, int64_t ldb, int64_t ldc,
-                              cudaStream_t stream) {
-  if (M <= 0 || N <= 0 || K < 0) return cudaErrorInvalidValue;
-  dim3 grid((N + TN - 1) / TN, (M + TM - 1) / TM);
-  gemm_simt_kernel<float><<<grid, 256, 0, stream>>>(A, B, C, nullptr, M, N, K, lda, ldb,
-                                                     ldc, 0, 1);
+cudaError_t launch_gemm_f32_simt(const GemmArgs &g, cudaStream_t stream) {
+  if (g.M <= 0 || g.N <= 0 || g.K < 0) return cudaErrorInvalidValue;
+  dim3 grid((g.N + TN - 1) / TN, (g.M + TM - 1) / TM);
+  if (grid.y > 65535) return cudaErrorInvalidValue;
+  gemm_simt_kernel<float><<<grid, 256, 0, stream>>>(
+      static_cast<const float *>(g.A), static_cast<const float *>(g.B), g.D, g.Cin, g.M, g.N,
+      g.K, g.lda, g.ldb, g.ldd, g.ldc, g.b_kn ? 1 : 0);
   return cudaGetLastError();
 }
 

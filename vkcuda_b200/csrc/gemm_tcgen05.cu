@@ -501,9 +501,11 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+}  // namespace
+
 bool make_map_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes,
                  const void *base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
-                 uint32_t box_inner, uint32_t box_outer) {
+                 uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   auto encode = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!encode) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -511,11 +513,13 @@ bool make_map_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes,
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(map, type, 2, const_cast<void *>(base), dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
+
+namespace {
 
 struct MapCache {
   GemmArgs key{};

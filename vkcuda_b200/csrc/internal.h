@@ -3,6 +3,7 @@
 // shape errors that the kernels cannot serve come back as
 // cudaErrorInvalidValue before anything is launched.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -56,10 +57,18 @@ struct GemmArgs {
 // meet its TMA requirements (then the caller uses the SIMT path).
 cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream);
 cudaError_t launch_gemm_simt(const GemmArgs &g, cudaStream_t stream);
-// fp32 SIMT C = A * B (the reference's matmulTiled, fp32 in and out).
-cudaError_t launch_matmul_f32(const float *A, const float *B, float *C, int M, int N,
-                              int K, int64_t lda, int64_t ldb, int64_t ldc,
-                              cudaStream_t stream);
+// fp32 in, fp32 out (A and B of `g` point to float; `g.bf16` is ignored):
+// the tensor-core path (three tf32 products per fp32 product, fp32-level
+// accuracy; cudaErrorNotSupported when strides / alignment break TMA's
+// 16-byte rule) and the CUDA-core path (any strides).
+cudaError_t launch_gemm_f32_tcgen05(const GemmArgs &g, cudaStream_t stream);
+cudaError_t launch_gemm_f32_simt(const GemmArgs &g, cudaStream_t stream);
+// 2-D tensor map over a row-major matrix of `outer` rows x `inner` elements
+// (row stride in elements), box box_inner x box_outer, zero fill outside.
+bool make_map_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes,
+                 const void *base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                 uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // ---- flash attention (flash_fwd_tcgen05.cu, flash_fwd_f32.cu)
 struct FlashArgs {
@@ -76,6 +85,7 @@ cudaError_t launch_flash_fwd_f32(const FlashArgs &f, cudaStream_t stream);
 // ---- device error words, one accessor per translation unit
 int stream_kernels_error(int clear);
 int gemm_tcgen05_error(int clear);
+int gemm_f32_error(int clear);
 int flash_tcgen05_error(int clear);
 int selftest_error(int clear);
 cudaError_t launch_selftest_bounded_wait(unsigned timeout_us, cudaStream_t stream);

@@ -95,6 +95,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   }
 }
 
+// As mbar_wait, with acquire at cluster scope: for a barrier that threads of
+// another CTA of the cluster release (mbar_arrive_cluster).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity,
+                                                  uint64_t limit_ns = 4000000000ull) {
+  const uint32_t addr = smem_u32(bar);
+  auto test = [&]() {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return done != 0;
+  };
+  if (test()) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    if (test()) return true;
+    if ((spin & 255u) == 0u && global_timer_ns() - t0 > limit_ns) {
+      record_error(kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map))
@@ -129,6 +156,18 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map,
   asm volatile(
       "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// 2D tiled reduce-add (element type of the map) of a shared-memory box into
+// global memory, completion tracked by the bulk-async group.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map,
+                                                  const void *smem_src, int32_t x,
+                                                  int32_t y) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
       "r"(smem_u32(smem_src)), "r"(x), "r"(y)
       : "memory");
 }
@@ -304,6 +343,24 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr,
   return d;
 }
 
+// Descriptor of a 32-bit MN-major operand in the layout TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B (layout type 1: 128-byte rows of 32
+// MN-elements, one per K index, whose 32-byte quarters are permuted by the
+// row index mod 4; the only swizzled MN-major layout kind::tf32 accepts):
+// LBO = byte distance between successive 32-element MN blocks, SBO = byte
+// distance between successive groups of 4 K-rows.
+__device__ __forceinline__ uint64_t smem_desc_sw128_atom32(uint32_t smem_addr,
+                                                           uint32_t lbo_bytes,
+                                                           uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= 1ull << 61;
+  return d;
+}
+
 // Instruction descriptor of tcgen05.mma kind::f16 with fp32 accumulation.
 //   bits 4-5 D format (1 = f32); bits 7-9 / 10-12 A / B format (0 f16, 1 bf16)
 //   bit 15 / 16 A / B major (0 = K-major, 1 = MN-major)
@@ -314,6 +371,15 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n,
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Instruction descriptor of tcgen05.mma kind::tf32 with fp32 accumulation:
+// as above with A / B format 2 (tf32: an fp32 bit pattern of which the MMA
+// uses sign, exponent and the top 10 mantissa bits).
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(uint32_t m, uint32_t n, bool a_mn_major,
+                                                      bool b_mn_major) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
 // ---------------------------------------------------------------- CTA pairs
@@ -381,6 +447,18 @@ __device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Pair MMA of kind::tf32 (K = 8 per instruction), issued by one thread of CTA 0.
+__device__ __forceinline__ void mma_tf32_ss_pair(uint32_t d_tmem, uint64_t a_desc,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -1145,6 +1145,17 @@ VCError gemm_dispatch(const vcb::GemmArgs &g, cudaStream_t s, const char *name) 
   return run(e, name);
 }
 
+// fp32 A, B: the tensor-core path (three tf32 products per product) when
+// TMA can take the strides, else the CUDA-core path.
+VCError gemm_f32_dispatch(const vcb::GemmArgs &g, cudaStream_t s, const char *name) {
+  cudaError_t e = vcb::launch_gemm_f32_tcgen05(g, s);
+  if (e == cudaErrorNotSupported) {
+    cudaGetLastError();
+    e = vcb::launch_gemm_f32_simt(g, s);
+  }
+  return run(e, name);
+}
+
 // wmma_gemm(A, B, C, D): D = A*B + C for one 8x8x16 tile
 // (test/wmma_gemm.vc:19-33): A 8x16 fp16 (ldm 16), B 16x8 fp16 (ldm 8), C/D
 // 8x8 fp32 (ldm 8).
@@ -1199,8 +1210,9 @@ VCError k_matmul_tiled(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, 
   const size_t nn = (size_t)N * N * 4;
   if (nn > bytes_available(A) || nn > bytes_available(B) || nn > bytes_available(C))
     return too_small("matmulTiled");
-  return run(vcb::launch_matmul_f32((const float *)A, (const float *)B, (float *)C, (int)rows,
-                                    (int)cols, (int)N, N, N, N, s), "matmulTiled");
+  vcb::GemmArgs g{A, B, (float *)C, nullptr, (int)rows, (int)cols, (int)N, N, N, N, 0,
+                  false, true};
+  return gemm_f32_dispatch(g, s, "matmulTiled");
 }
 
 // ---- native entries (explicit shapes; grid and block are not used)
@@ -1265,18 +1277,21 @@ VCError k_native_block_reduce(VCKernel &, const LaunchShape &, const VCKernelArg
 }
 
 VCError gemm_checked(const vcb::GemmArgs &g, int dtype, cudaStream_t s) {
-  if (dtype != VC_DTYPE_F16 && dtype != VC_DTYPE_BF16) return VCError::InvalidValue;
+  if (dtype != VC_DTYPE_F16 && dtype != VC_DTYPE_BF16 && dtype != VC_DTYPE_F32)
+    return VCError::InvalidValue;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0) return VCError::InvalidValue;
   if (g.lda < g.K || g.ldd < g.N || (g.b_kn ? g.ldb < g.N : g.ldb < g.K)) return VCError::InvalidValue;
   if (g.Cin && g.ldc < g.N) return VCError::InvalidValue;
-  const size_t a_need = ((size_t)(g.M - 1) * g.lda + g.K) * 2;
-  const size_t b_need = g.b_kn ? ((size_t)(g.K - 1) * g.ldb + g.N) * 2
-                               : ((size_t)(g.N - 1) * g.ldb + g.K) * 2;
+  const size_t esz = dtype == VC_DTYPE_F32 ? 4 : 2;
+  const size_t a_need = ((size_t)(g.M - 1) * g.lda + g.K) * esz;
+  const size_t b_need = g.b_kn ? ((size_t)(g.K - 1) * g.ldb + g.N) * esz
+                               : ((size_t)(g.N - 1) * g.ldb + g.K) * esz;
   const size_t d_need = ((size_t)(g.M - 1) * g.ldd + g.N) * 4;
   if (a_need > bytes_available(g.A) || b_need > bytes_available(g.B) || d_need > bytes_available(g.D))
     return too_small("vc.gemm");
   if (g.Cin && ((size_t)(g.M - 1) * g.ldc + g.N) * 4 > bytes_available(g.Cin))
     return too_small("vc.gemm");
+  if (dtype == VC_DTYPE_F32) return gemm_f32_dispatch(g, s, "vc.gemm");
   return gemm_dispatch(g, s, "vc.gemm");
 }
 
@@ -1665,8 +1680,9 @@ int vc_kernel_set_constant(void *k, const char *name, long long value) {
 int vc_kernel_error(int clear) {
   if (!ensure_init()) return E(VCError::InitializationError);
   use_current_device();
-  int codes[4] = {vcb::stream_kernels_error(clear), vcb::gemm_tcgen05_error(clear),
-                  vcb::flash_tcgen05_error(clear), vcb::selftest_error(clear)};
+  int codes[5] = {vcb::stream_kernels_error(clear), vcb::gemm_tcgen05_error(clear),
+                  vcb::gemm_f32_error(clear), vcb::flash_tcgen05_error(clear),
+                  vcb::selftest_error(clear)};
   for (int c : codes)
     if (c != 0) return c;
   return 0;
