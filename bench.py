@@ -1,7 +1,7 @@
 """Benchmark of the B200 hot path behind the VC runtime API.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--only gemm,fa_causal,fa_bf16,stream,fa_f32]
+                    [--only gemm,fa_causal,fa_bf16,stream,fa_f32,gemm_f32]
 
 One JSON line on rank 0. The headline workload is the dense GEMM
 C = A*B, M = N = K = 4096, fp16 inputs drawn U[-1, 1), fp32 accumulate and
@@ -17,6 +17,9 @@ The other benchmark configurations ride along in "also":
              NVLink (an NCCL all-reduce after the kernel is timed beside it)
   fa_f32     flash-attention fwd fp32, B=1, H=1, N=256, d=64 (the demo's
              precision; latency bound)
+  gemm_f32   fp32 GEMM 4096^3 (the fp32 demo kernel's contract) on the tensor
+             cores, three tf32 products per product; the CUDA-core path of
+             the same call timed beside it
 Under torchrun (N > 1) ranks time on the device with CUDA events between
 barriers; rank 0 prints the max over ranks.
 
@@ -378,6 +381,85 @@ def gemm_e2e(vc, dist, steps, warmup):
                     "steps alternating over two streams"}
 
 
+def gemm_f32_workload(vc, dist, steps, warmup, pk):
+    """fp32 C = A * B at 4096^3 (the reference's fp32 GEMM, matmulTiled in
+    examples/matmul_bench.vc, at the headline size): tensor-core path, three
+    tf32 products per fp32 product. Reported as fp32 TFLOP/s delivered; the
+    roofline counts the tensor pipe's 3 x 2 N^3 tf32 FLOP against the dense
+    tf32 rate (half the fp16/bf16 rate). The CUDA-core path of the same API
+    (taken for strides TMA cannot serve: lda = N + 1) is timed beside it."""
+    import torch
+    N, per_step = 4096, 16
+    g = torch.Generator(device="cuda").manual_seed(11 + dist.rank)
+    sets = []
+    for _ in range(2):  # 192 MiB per set > 126 MB L2
+        A = torch.rand(N, N, device="cuda", generator=g) * 2 - 1
+        B = torch.rand(N, N, device="cuda", generator=g) * 2 - 1
+        sets.append((A, B, torch.empty(N, N, device="cuda")))
+    stream = torch.cuda.current_stream()
+    state = {"i": 0}
+
+    def one():
+        A, B, C = sets[state["i"] % 2]
+        state["i"] += 1
+        check(vc.gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), None, N, N, N, N, N, N, 0,
+                      vc.Dtype.F32, True, stream.cuda_stream), "vc_gemm f32")
+
+    def step():
+        for _ in range(per_step):
+            one()
+
+    one()
+    torch.cuda.synchronize()
+    A, B, C = sets[0]
+    ref = A[:64].double() @ B.double()
+    mag = A[:64].abs().double() @ B.abs().double()
+    perr = ((C[:64].double() - ref).abs() / mag).max().item()
+    if not perr <= 2e-5:
+        raise RuntimeError(f"fp32 GEMM parity guard failed: {perr}")
+    step_stats = {}
+    ms = timed(dist, stream, step, steps, warmup, stats=step_stats)
+    per_launch = ms / (steps * per_step)
+    value = 2.0 * N ** 3 * dist.world / (per_launch * 1e-3) / 1e12
+    achieved = 3 * 2.0 * N ** 3 / (per_launch * 1e-3) / 1e12
+    sustained = ms > 200.0
+    peak = round((pk["bf16_sustained"] if sustained else pk["bf16"]) / 2, 1)
+    # CUDA-core path of the same call: A with a row stride of N + 1 floats.
+    Ap = torch.zeros(N, N + 1, device="cuda")
+    Ap[:, :N] = A
+
+    def simt():
+        check(vc.gemm(Ap.data_ptr(), B.data_ptr(), C.data_ptr(), None, N, N, N, N + 1, N, N, 0,
+                      vc.Dtype.F32, True, stream.cuda_stream), "vc_gemm f32 simt")
+
+    simt()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(3):
+        simt()
+    e1.record()
+    torch.cuda.synchronize()
+    simt_ms = e0.elapsed_time(e1) / 3
+    res = {"workload": "gemm_f32", "value": round(value, 2), "unit": "TFLOP/s",
+           "ms_per_step": round(ms / steps, 4), "per_launch_ms": round(per_launch, 4),
+           "ms_per_step_median": step_stats["median_ms"], "ms_per_step_best": step_stats["best_ms"],
+           "scaling": "weak",
+           "config": {"M": N, "N": N, "K": N, "dtype": "f32", "layout": "row-major, B [K][N]",
+                      "gemms_per_step": per_step, "method": "3 tf32 products per product, "
+                      "512-deep K chunks added with round-to-nearest"},
+           "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                        "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                        "peak_kind": "tf32 dense = half the measured bf16 "
+                        + ("sustained" if sustained else "burst") + f" ({pk['source']})",
+                        "traffic": traffic_table().get("gemm_f32_4096")},
+           "simt_path_tflops": round(2.0 * N ** 3 / (simt_ms * 1e-3) / 1e12, 2),
+           "gpu_launches": steps * per_step, "parity_guard_max_rel_err": perr}
+    del sets, Ap
+    torch.cuda.empty_cache()
+    return res
+
+
 def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk, shard_bh):
     import torch
     BH = B * H
@@ -556,7 +638,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default="gemm,fa_causal,fa_bf16,stream,fa_f32")
+    ap.add_argument("--only", default="gemm,fa_causal,fa_bf16,stream,fa_f32,gemm_f32")
     ap.add_argument("--fa-bf16-heads", type=int, default=32,
                     help="heads of the bf16 attention config (32); a smaller count gives a "
                          "launch small enough for an ncu capture, whose DRAM traffic scales "
@@ -616,7 +698,9 @@ def main():
                                                args.stream_log2n)),
             ("fa_f32", lambda: flash_workload(vc, dist, "fa_f32", 1, 1, 256, 64, False,
                                               vc.Dtype.F32, max(args.steps, 20), args.warmup, pk,
-                                              shard_bh=False))]
+                                              shard_bh=False)),
+            ("gemm_f32", lambda: gemm_f32_workload(vc, dist, max(3, min(args.steps, 10)),
+                                                   args.warmup, pk))]
     for name, fn in jobs:
         if name in only:
             try:

@@ -66,8 +66,10 @@ def test_matmul_tiled_demo_sizes_relative_1e4(gpu, dev, orc, N):
     ref = orc.gemm(A, B, N, N, N, N, N, True)
     rel = np.abs(got - ref) / np.where(ref != 0, np.abs(ref), 1.0)
     assert rel.max() <= 1e-4, rel.max()
-    # far inside the demo's bar: the split product is near fp32 accuracy
-    assert rel.max() <= 1e-5, rel.max()
+    # inside the demo's bar with room: the tensor cores' truncating fp32
+    # accumulation is bounded to one 512-deep K chunk (same-sign data shows
+    # its bias in full), the chunks are added with round-to-nearest
+    assert rel.max() <= 3e-5, rel.max()
     gpu.vcReleaseKernel(k)
 
 

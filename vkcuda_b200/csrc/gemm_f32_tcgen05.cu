@@ -12,21 +12,25 @@
 // accumulate lo_a*hi_b + hi_a*lo_b + hi_a*hi_b in fp32 with tcgen05.mma
 // kind::tf32. The MMA reads lo to tf32 precision, and the dropped lo_a*lo_b
 // term is below 2^-20 |a*b|, so each product carries ~2^-19 relative error
-// against ~2^-24 for an fp32 FMA: far inside 1e-4 at any K the demos use.
-// Non-finite x keeps hi = x, lo = 0; an infinity then meets the other
-// operand's lo (usually 0) and its outputs read NaN where fp32 FMA gives inf.
+// against ~2^-24 for an fp32 FMA. hi is never written: kind::tf32 uses only
+// sign, exponent and the top 10 mantissa bits of each fp32 operand (measured:
+// the raw tile in place of an explicit hi leaves the error at 2e-7 of
+// sum|a*b| at 4096^3, where an MMA that rounded its inputs would leave
+// errors near 2^-11), so the raw tile serves as hi and only lo is written.
+// Non-finite x gets lo = 0; an infinity then meets the other operand's lo
+// (usually 0) and its outputs read NaN where fp32 FMA gives inf.
 //
 // Design: CTA pairs (cluster of two, cta_group::2), 256 x 256 output tiles,
-// one persistent cluster per SM pair, 320 threads per CTA:
+// one persistent cluster per SM pair, 448 threads per CTA:
 //   warp 0      TMA producer (each CTA): per 32-deep K stage, this CTA's 128
 //               rows of A (128 x 32 fp32 = 16 KiB) and its 128-column half of
 //               the B panel (16 KiB), 128-byte swizzled, 3-stage ring.
-//   warps 6..9  split (each CTA): once a stage lands, rewrite it in place as
-//               hi and write lo beside it (same swizzled layout), fence the
-//               writes to the tensor proxy, arrive on CTA 0's split barrier.
+//   warps 6..13 split (each CTA): once a stage lands, write lo beside it
+//               (same swizzled layout), fence the writes to the tensor proxy,
+//               arrive on CTA 0's split barrier.
 //   warp 1      CTA 0 lane 0 issues 3 pair MMAs (M = 256, N = 256, K = 8)
 //               per 8-deep K step from both CTAs' shared memory into TMEM
-//               (2 x 256-column accumulators, one per 256-deep K chunk,
+//               (2 x 256-column accumulators, one per 512-deep K chunk,
 //               alternating); its commits free the stage in both CTAs and
 //               hand each chunk to the epilogues.
 //   warps 2..5  epilogue (each CTA): tcgen05.ld of its 128 accumulator rows,
@@ -34,7 +38,7 @@
 //               the optional Cin addend) and TMA reduce-added for the rest.
 // B stored [K][N] (the demos' layout) is an MN-major operand; for tf32 that
 // takes the 128-byte swizzle with 32-byte atoms, in TMA and descriptor.
-// Shared memory per stage: A raw/hi, B raw/hi, A lo, B lo = 64 KiB; 3 stages
+// Shared memory per stage: A raw, B raw, A lo, B lo = 64 KiB; 3 stages
 // + 32 KiB of epilogue staging = 224 KiB. Ragged M, N, K: TMA zero-fills
 // loads outside the matrix (zero splits into zero hi and lo) and clips
 // stores. Roofline: 3 x 2*M*N*K tf32 FLOP on the tensor pipe, whose dense
@@ -61,9 +65,9 @@ constexpr int kAccCols = BN;
 constexpr uint32_t kTmemCols = 2 * kAccCols;
 constexpr int kEpiCols = 32;
 constexpr uint32_t kEpiBytes = BM * kEpiCols * 4;
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
 constexpr int kEpiThreads = 128;
-constexpr int kSplitWarps = 4;
+constexpr int kSplitWarps = 8;
 constexpr int kSplitThreads = kSplitWarps * 32;
 constexpr int kSplitChunks = kRawBytes / 16 / kSplitThreads;  // 16-byte chunks per thread
 constexpr int kGroupRows = 8;
@@ -73,8 +77,10 @@ constexpr size_t kGroupAboveBBytes = 64ull << 20;
 // same-sign data, growing with K). So each tile accumulates K in chunks of
 // kChunkK in TMEM, and the epilogue adds the chunks into D with round-to-
 // nearest reduce-adds (TMA bulk reduce), bounding the truncation to one
-// chunk's worth.
-constexpr int kChunkK = 256;
+// chunk's worth. Measured at 4096^3: chunks of 256 / 512 / 1024 run at
+// 178 / 188 / 194 TFLOP/s (each chunk's staging and reduce traffic shares
+// shared memory with the mainloop); 512 keeps the same-sign error near 1e-5.
+constexpr int kChunkK = 512;
 
 struct __align__(8) F32Barriers {
   uint64_t full[kStages];    // each CTA: its own TMA bytes landed
@@ -90,11 +96,10 @@ constexpr size_t kSmemBytes =
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kRawBytes % (16 * kSplitThreads) == 0, "split work divides evenly");
 
-// hi: x with the low 13 mantissa bits cleared; lo = x - hi (exact).
-__device__ __forceinline__ void split_tf32(uint32_t x, uint32_t &hi, uint32_t &lo) {
+// lo = x - hi with hi = x with the low 13 mantissa bits cleared (exact).
+__device__ __forceinline__ uint32_t tf32_lo(uint32_t x) {
   const bool finite = (x & 0x7f800000u) != 0x7f800000u;
-  hi = finite ? (x & 0xffffe000u) : x;
-  lo = finite ? __float_as_uint(__uint_as_float(x) - __uint_as_float(hi)) : 0u;
+  return finite ? __float_as_uint(__uint_as_float(x) - __uint_as_float(x & 0xffffe000u)) : 0u;
 }
 
 // Stage this warp's 32 x 32 box (128-byte swizzle, as the D map) and store
@@ -285,25 +290,20 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     for (int u = cluster; ok && u < num_units; u += num_clusters) {
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!__all_sync(0xffffffffu, mbar_wait(&bars->full[stage], phase))) { ok = false; break; }
-        uint8_t *raw = stage_base + stage * kStageBytes;
+        // Consecutive lanes take consecutive 16-byte chunks: each quarter
+        // warp covers one 128-byte row, all 32 banks.
+        const uint32_t raw = smem_u32(stage_base + stage * kStageBytes) + t * 16;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint4 v[kSplitChunks / 2];
 #pragma unroll
           for (int i = 0; i < kSplitChunks / 2; ++i)
-            v[i] = *reinterpret_cast<const uint4 *>(
-                raw + ((half * (kSplitChunks / 2) + i) * kSplitThreads + t) * 16);
+            v[i] = lds128(raw + (half * (kSplitChunks / 2) + i) * kSplitThreads * 16);
 #pragma unroll
-          for (int i = 0; i < kSplitChunks / 2; ++i) {
-            uint4 hi, lo;
-            split_tf32(v[i].x, hi.x, lo.x);
-            split_tf32(v[i].y, hi.y, lo.y);
-            split_tf32(v[i].z, hi.z, lo.z);
-            split_tf32(v[i].w, hi.w, lo.w);
-            const uint32_t off = ((half * (kSplitChunks / 2) + i) * kSplitThreads + t) * 16;
-            *reinterpret_cast<uint4 *>(raw + off) = hi;
-            *reinterpret_cast<uint4 *>(raw + kRawBytes + off) = lo;
-          }
+          for (int i = 0; i < kSplitChunks / 2; ++i)
+            sts128(raw + kRawBytes + (half * (kSplitChunks / 2) + i) * kSplitThreads * 16,
+                   make_uint4(tf32_lo(v[i].x), tf32_lo(v[i].y), tf32_lo(v[i].z),
+                              tf32_lo(v[i].w)));
         }
         fence_proxy_async_smem();
         __syncwarp();
