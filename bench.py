@@ -18,8 +18,8 @@ The other benchmark configurations ride along in "also":
   fa_f32     flash-attention fwd fp32, B=1, H=1, N=256, d=64 (the demo's
              precision; latency bound)
   gemm_f32   fp32 GEMM 4096^3 (the fp32 demo kernel's contract) on the tensor
-             cores, three tf32 products per product; the CUDA-core path of
-             the same call timed beside it
+             cores from a hi/lo split (hi*hi in tf32, corrections in bf16);
+             the CUDA-core path of the same call timed beside it
 Under torchrun (N > 1) ranks time on the device with CUDA events between
 barriers; rank 0 prints the max over ranks.
 
@@ -411,11 +411,13 @@ def gemm_e2e(vc, dist, steps, warmup):
 
 def gemm_f32_workload(vc, dist, steps, warmup, pk):
     """fp32 C = A * B at 4096^3 (the reference's fp32 GEMM, matmulTiled in
-    examples/matmul_bench.vc, at the headline size): tensor-core path, three
-    tf32 products per fp32 product. Reported as fp32 TFLOP/s delivered; the
-    roofline counts the tensor pipe's 3 x 2 N^3 tf32 FLOP against the dense
-    tf32 rate (half the fp16/bf16 rate). The CUDA-core path of the same API
-    (taken for strides TMA cannot serve: lda = N + 1) is timed beside it."""
+    examples/matmul_bench.vc, at the headline size): tensor-core path, hi*hi
+    as one tf32 MMA and lo*hi + hi*lo as one bf16 MMA per 8-deep K step.
+    Reported as fp32 TFLOP/s delivered; the roofline counts the tensor pipe's
+    work as 4 N^3 tf32-equivalent FLOP (2 N^3 tf32 + 4 N^3 bf16 at twice the
+    rate) against the dense tf32 rate (half the fp16/bf16 rate). The
+    CUDA-core path of the same API (taken for strides TMA cannot serve:
+    lda = N + 1) is timed beside it."""
     import torch
     N, per_step = 4096, 16
     g = torch.Generator(device="cuda").manual_seed(11 + dist.rank)
@@ -449,7 +451,7 @@ def gemm_f32_workload(vc, dist, steps, warmup, pk):
     ms = timed(dist, stream, step, steps, warmup, stats=step_stats)
     per_launch = ms / (steps * per_step)
     value = 2.0 * N ** 3 * dist.world / (per_launch * 1e-3) / 1e12
-    achieved = 3 * 2.0 * N ** 3 / (per_launch * 1e-3) / 1e12
+    achieved = 4.0 * N ** 3 / (per_launch * 1e-3) / 1e12
     sustained = ms > 200.0
     peak = round((pk["bf16_sustained"] if sustained else pk["bf16"]) / 2, 1)
     # CUDA-core path of the same call: A with a row stride of N + 1 floats.
@@ -474,11 +476,11 @@ def gemm_f32_workload(vc, dist, steps, warmup, pk):
            "ms_per_step_median": step_stats["median_ms"], "ms_per_step_best": step_stats["best_ms"],
            "scaling": "weak",
            "config": {"M": N, "N": N, "K": N, "dtype": "f32", "layout": "row-major, B [K][N]",
-                      "gemms_per_step": per_step, "method": "3 tf32 products per product, "
-                      "512-deep K chunks added with round-to-nearest"},
+                      "gemms_per_step": per_step, "method": "hi/lo split: hi*hi tf32, "
+                      "lo*hi + hi*lo bf16; 512-deep K chunks added with round-to-nearest"},
            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                        "peak_kind": "tf32 dense = half the measured bf16 "
+                        "peak_kind": "tf32-equivalent work 4 N^3; tf32 dense = half the measured bf16 "
                         + ("sustained" if sustained else "burst") + f" ({pk['source']})",
                         "traffic": traffic_table().get("gemm_f32_4096")},
            "simt_path_tflops": round(2.0 * N ** 3 / (simt_ms * 1e-3) / 1e12, 2),

@@ -224,9 +224,10 @@ int vc_block_reduce_f32(const float *in, float *out, int n, int block,
  * row-major. dtype VC_DTYPE_F16 or VC_DTYPE_BF16, fp32 accumulate.
  * Replaces wmma_gemm (test/wmma_gemm.vc:19-33) and matmulCoopmat
  * (examples/matmul_coopmat_bench.vc:60-110).
- * dtype VC_DTYPE_F32: A and B are fp32, computed on the tensor cores as three
- * tf32 products per fp32 product (fp32-level accuracy, about 2^-19 relative
- * per product); replaces matmulTiled (examples/matmul_bench.vc:22-54). */
+ * dtype VC_DTYPE_F32: A and B are fp32, computed on the tensor cores from a
+ * hi/lo split of each operand (hi*hi in tf32, the two correction products in
+ * bf16; at most ~2^-17 relative per product, rounded to nearest); replaces
+ * matmulTiled (examples/matmul_bench.vc:22-54). */
 int vc_gemm(const void *A, const void *B, float *D, const float *Cin, int M,
             int N, int K, int64_t lda, int64_t ldb, int64_t ldd, int64_t ldc,
             int dtype, int b_kn, void *stream);

@@ -6,44 +6,55 @@
 // and B through shared memory, fp32 multiply-add over K), whose bar is 1e-4
 // relative error against an fp64 loop (matmul_bench.vc:109-125).
 //
-// Method (the three-term tf32 split product, "3xTF32"): every fp32 operand x
-// is split into hi = x with its low 13 mantissa bits cleared (exactly a tf32
-// value) and lo = x - hi (exact in fp32, |lo| < 2^-10 |x|); the tensor cores
-// accumulate lo_a*hi_b + hi_a*lo_b + hi_a*hi_b in fp32 with tcgen05.mma
-// kind::tf32. The MMA reads lo to tf32 precision, and the dropped lo_a*lo_b
-// term is below 2^-20 |a*b|, so each product carries ~2^-19 relative error
-// against ~2^-24 for an fp32 FMA. hi is never written: kind::tf32 uses only
-// sign, exponent and the top 10 mantissa bits of each fp32 operand (measured:
-// the raw tile in place of an explicit hi leaves the error at 2e-7 of
-// sum|a*b| at 4096^3, where an MMA that rounded its inputs would leave
-// errors near 2^-11), so the raw tile serves as hi and only lo is written.
-// Non-finite x gets lo = 0; an infinity then meets the other operand's lo
-// (usually 0) and its outputs read NaN where fp32 FMA gives inf.
+// Method (a three-term split product): every fp32 operand x is split into
+// hi = x with its low 13 mantissa bits cleared (exactly a tf32 value) and
+// lo = x - hi (exact in fp32, |lo| < 2^-10 |x|), and the tensor cores
+// accumulate hi_a*hi_b + (lo_a*hi_b + hi_a*lo_b) in fp32:
+//   * hi_a*hi_b with tcgen05.mma kind::tf32 straight from the raw fp32
+//     tiles: kind::tf32 uses only sign, exponent and the top 10 mantissa
+//     bits of each operand (measured: the raw tile in place of an explicit
+//     hi leaves the error unchanged, where an MMA that rounded its inputs
+//     would leave errors near 2^-11), so hi is never written;
+//   * both correction terms with one kind::f16 MMA (bf16, K = 16) per 8-deep
+//     K step over packed tiles that hold, per group of 8 K indices, [lo | hi]
+//     of A against [hi ; lo] of B, rounded to bf16 (2^-9 relative): 2 MMAs
+//     per 8-deep step instead of the 3 of an all-tf32 split, and the 16-bit
+//     operands halve the tensor cores' shared-memory reads for them.
+// Each correction term is below 2^-10 |a*b| and carries <= 2^-8 of itself,
+// the dropped lo_a*lo_b is below 2^-20 |a*b|: <= ~2^-17 |a*b| per product,
+// round-to-nearest (unbiased), against 2^-24 for an fp32 FMA; far inside the
+// reference's 1e-4. Non-finite inputs give NaN outputs (an infinity meets a
+// zero low part), where an fp32 FMA loop would give inf for an infinity.
 //
 // Design: CTA pairs (cluster of two, cta_group::2), 256 x 256 output tiles,
-// one persistent cluster per SM pair, 448 threads per CTA:
-//   warp 0      TMA producer (each CTA): per 32-deep K stage, this CTA's 128
-//               rows of A (128 x 32 fp32 = 16 KiB) and its 128-column half of
-//               the B panel (16 KiB), 128-byte swizzled, 3-stage ring.
-//   warps 6..13 split (each CTA): once a stage lands, write lo beside it
-//               (same swizzled layout), fence the writes to the tensor proxy,
-//               arrive on CTA 0's split barrier.
-//   warp 1      CTA 0 lane 0 issues 3 pair MMAs (M = 256, N = 256, K = 8)
-//               per 8-deep K step from both CTAs' shared memory into TMEM
-//               (2 x 256-column accumulators, one per 512-deep K chunk,
-//               alternating); its commits free the stage in both CTAs and
-//               hand each chunk to the epilogues.
-//   warps 2..5  epilogue (each CTA): tcgen05.ld of its 128 accumulator rows,
-//               32 x 32 swizzled boxes TMA-stored for the first K chunk (with
-//               the optional Cin addend) and TMA reduce-added for the rest.
+// one persistent cluster per SM pair, 704 threads per CTA:
+//   warp 0       TMA producer (each CTA): per 32-deep K stage, this CTA's 128
+//                rows of A (128 x 32 fp32 = 16 KiB) and its 128-column half
+//                of the B panel (16 KiB), swizzled, 3-stage ring.
+//   warps 6..21  split (each CTA): once a stage lands, write the packed bf16
+//                hi/lo tiles beside it (128-byte swizzled, 128-bit shared
+//                accesses laid out so every quarter warp hits 32 banks),
+//                fence the writes to the tensor proxy, arrive on CTA 0's
+//                split barrier.
+//   warp 1       CTA 0 lane 0 issues, per 8-deep K step, a tf32 pair MMA and
+//                a bf16 pair MMA (M = 256, N = 256) from both CTAs' shared
+//                memory into TMEM (2 x 256-column accumulators, one per
+//                512-deep K chunk, alternating); its commits free the stage
+//                in both CTAs and hand each chunk to the epilogues.
+//   warps 2..5   epilogue (each CTA): tcgen05.ld of its 128 accumulator rows,
+//                32 x 32 swizzled boxes TMA-stored for the first K chunk
+//                (with the optional Cin addend) and TMA reduce-added for the
+//                rest.
 // B stored [K][N] (the demos' layout) is an MN-major operand; for tf32 that
 // takes the 128-byte swizzle with 32-byte atoms, in TMA and descriptor.
-// Shared memory per stage: A raw, B raw, A lo, B lo = 64 KiB; 3 stages
-// + 32 KiB of epilogue staging = 224 KiB. Ragged M, N, K: TMA zero-fills
-// loads outside the matrix (zero splits into zero hi and lo) and clips
-// stores. Roofline: 3 x 2*M*N*K tf32 FLOP on the tensor pipe, whose dense
-// rate is half the fp16 rate; 2*M*N*K fp32 FLOP delivered.
+// Shared memory per stage: A raw, B raw, A packed, B packed = 64 KiB; 3
+// stages + 32 KiB of epilogue staging = 224 KiB. Ragged M, N, K: TMA
+// zero-fills loads outside the matrix and clips stores. Roofline: per
+// 2*M*N*K fp32 FLOP delivered, the tensor pipe runs 2*M*N*K tf32 and
+// 2*2*M*N*K bf16 FLOP; dense tf32 runs at half the bf16 rate, so the
+// tensor-pipe time equals that of 4*M*N*K tf32 FLOP ("tf32-equivalent").
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <mutex>
@@ -65,11 +76,13 @@ constexpr int kAccCols = BN;
 constexpr uint32_t kTmemCols = 2 * kAccCols;
 constexpr int kEpiCols = 32;
 constexpr uint32_t kEpiBytes = BM * kEpiCols * 4;
-constexpr int kThreads = 448;
 constexpr int kEpiThreads = 128;
-constexpr int kSplitWarps = 8;
+constexpr int kSplitWarps = 16;
+// Warps: 0 TMA, 1 MMA, 2..5 epilogue, then the split warps.
+constexpr int kFirstSplitWarp = 6;
+constexpr int kThreads = (kFirstSplitWarp + kSplitWarps) * 32;
 constexpr int kSplitThreads = kSplitWarps * 32;
-constexpr int kSplitChunks = kRawBytes / 16 / kSplitThreads;  // 16-byte chunks per thread
+constexpr int kUnitsPerThread = kTileBytes / 32 / kSplitThreads;  // per operand, per stage
 constexpr int kGroupRows = 8;
 constexpr size_t kGroupAboveBBytes = 64ull << 20;
 // The tensor cores' fp32 accumulation truncates: a running sum loses about
@@ -77,9 +90,10 @@ constexpr size_t kGroupAboveBBytes = 64ull << 20;
 // same-sign data, growing with K). So each tile accumulates K in chunks of
 // kChunkK in TMEM, and the epilogue adds the chunks into D with round-to-
 // nearest reduce-adds (TMA bulk reduce), bounding the truncation to one
-// chunk's worth. Measured at 4096^3: chunks of 256 / 512 / 1024 run at
-// 178 / 188 / 194 TFLOP/s (each chunk's staging and reduce traffic shares
-// shared memory with the mainloop); 512 keeps the same-sign error near 1e-5.
+// chunk's worth. Measured at 4096^3 (all-tf32 split): chunks of 256 / 512 /
+// 1024 ran at 178 / 188 / 194 TFLOP/s (each chunk's staging and reduce
+// traffic shares shared memory with the mainloop); 512 keeps the same-sign
+// error near 1e-5.
 constexpr int kChunkK = 512;
 
 struct __align__(8) F32Barriers {
@@ -94,12 +108,33 @@ struct __align__(8) F32Barriers {
 constexpr size_t kSmemBytes =
     1024 + kStages * kStageBytes + 2 * kEpiBytes + sizeof(F32Barriers);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
-static_assert(kRawBytes % (16 * kSplitThreads) == 0, "split work divides evenly");
+static_assert(kTileBytes % (32 * kSplitThreads) == 0, "split work divides evenly");
 
-// lo = x - hi with hi = x with the low 13 mantissa bits cleared (exact).
-__device__ __forceinline__ uint32_t tf32_lo(uint32_t x) {
-  const bool finite = (x & 0x7f800000u) != 0x7f800000u;
-  return finite ? __float_as_uint(__uint_as_float(x) - __uint_as_float(x & 0xffffe000u)) : 0u;
+// hi = x with the low 13 mantissa bits cleared (the tf32 value the MMA
+// reads), lo = x - hi (exact for finite x; NaN for non-finite x, whose
+// outputs are NaN either way).
+__device__ __forceinline__ void split_tf32(uint32_t x, float &hi, float &lo) {
+  hi = __uint_as_float(x & 0xffffe000u);
+  lo = __uint_as_float(x) - hi;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float first, float second) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(first, second);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// 8 consecutive fp32 values (p0, p1) -> their hi and lo parts as 8 bf16
+// each (round to nearest), in the same order.
+__device__ __forceinline__ void split8_bf16(const uint4 &p0, const uint4 &p1, uint4 &hi,
+                                            uint4 &lo) {
+  const uint32_t x[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+  float h[8], l[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) split_tf32(x[e], h[e], l[e]);
+  hi = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
+                  pack_bf16x2(h[6], h[7]));
+  lo = make_uint4(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]), pack_bf16x2(l[4], l[5]),
+                  pack_bf16x2(l[6], l[7]));
 }
 
 // Stage this warp's 32 x 32 box (128-byte swizzle, as the D map) and store
@@ -130,8 +165,9 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmD,
                      const float *__restrict__ Cin, int64_t ldc, int M, int N, int K,
-                     uint32_t idesc_full, uint32_t idesc_half, int b_kn, int num_full,
-                     int num_units, int group_rows, int chunk_kblocks) {
+                     uint32_t idesc_full, uint32_t idesc_half, uint32_t idesc16_full,
+                     uint32_t idesc16_half, int b_kn, int num_full, int num_units,
+                     int group_rows, int chunk_kblocks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -242,6 +278,7 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         const uint32_t idesc = (u < num_full) ? idesc_full : idesc_half;
+        const uint32_t idesc16 = (u < num_full) ? idesc16_full : idesc16_half;
         if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kAccCols;
@@ -251,25 +288,28 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
           // the tensor proxy before its release arrive) precede these MMAs.
           if (!mbar_wait_cluster(&bars->split[stage], phase)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_hi = smem_u32(stage_base + stage * kStageBytes);
-          const uint32_t b_hi = a_hi + kTileBytes;
-          const uint32_t a_lo = a_hi + kRawBytes;
-          const uint32_t b_lo = b_hi + kRawBytes;
+          const uint32_t a_raw = smem_u32(stage_base + stage * kStageBytes);
+          const uint32_t b_raw = a_raw + kTileBytes;
+          const uint32_t a_pk = a_raw + kRawBytes;
+          const uint32_t b_pk = b_raw + kRawBytes;
 #pragma unroll
-          for (int k = 0; k < BK / 8; ++k) {
-            // K-major: 8 fp32 = 32 bytes per step inside the swizzle row.
-            // MN-major B (32-byte-atom swizzle): 8 K-rows = 1024 bytes per
-            // step, 4-row groups 512 bytes apart, 32-column blocks BK x 128
-            // bytes apart.
-            const uint64_t adh = smem_desc_sw128(a_hi + k * 32, 16, 1024);
-            const uint64_t adl = smem_desc_sw128(a_lo + k * 32, 16, 1024);
-            const uint64_t bdh = b_kn ? smem_desc_sw128_atom32(b_hi + k * 1024, BK * 128, 512)
-                                      : smem_desc_sw128(b_hi + k * 32, 16, 1024);
-            const uint64_t bdl = b_kn ? smem_desc_sw128_atom32(b_lo + k * 1024, BK * 128, 512)
-                                      : smem_desc_sw128(b_lo + k * 32, 16, 1024);
-            mma_tf32_ss_pair(d_tmem, adl, bdh, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
-            mma_tf32_ss_pair(d_tmem, adh, bdl, idesc, 1u);
-            mma_tf32_ss_pair(d_tmem, adh, bdh, idesc, 1u);
+          for (int g = 0; g < BK / 8; ++g) {
+            // hi*hi: tf32 from the raw tiles. K-major: 8 fp32 = 32 bytes per
+            // step inside the swizzle row. MN-major B (32-byte-atom
+            // swizzle): 8 K-rows = 1024 bytes per step, 4-row groups 512
+            // bytes apart, 32-column blocks BK x 128 bytes apart.
+            const uint64_t ad = smem_desc_sw128(a_raw + g * 32, 16, 1024);
+            const uint64_t bd = b_kn ? smem_desc_sw128_atom32(b_raw + g * 1024, BK * 128, 512)
+                                     : smem_desc_sw128(b_raw + g * 32, 16, 1024);
+            // lo*hi + hi*lo: one bf16 MMA of K = 16 over the packed tiles.
+            // K-major: 16 bf16 = 32 bytes per step. MN-major B: 16 K-rows =
+            // 2048 bytes per step, 8-row groups 1024 apart, 64-column blocks
+            // 64 x 128 bytes apart.
+            const uint64_t apd = smem_desc_sw128(a_pk + g * 32, 16, 1024);
+            const uint64_t bpd = b_kn ? smem_desc_sw128(b_pk + g * 2048, 64 * 128, 1024)
+                                      : smem_desc_sw128(b_pk + g * 32, 16, 1024);
+            mma_tf32_ss_pair(d_tmem, ad, bd, idesc, (kb != kb0 || g != 0) ? 1u : 0u);
+            mma_f16_ss_pair(d_tmem, apd, bpd, idesc16, 1u);
           }
           mma_commit_pair(lead(&bars->empty[stage]));
           mma_commit_pair(peer(&bars->empty[stage]));
@@ -281,29 +321,65 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
        }
       }
     }
-  } else if (warp >= 6) {
+  } else if (warp >= kFirstSplitWarp) {
     // ---------------- split warps (each CTA)
-    const int t = threadIdx.x - 6 * 32;
+    const int t = threadIdx.x - kFirstSplitWarp * 32;
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     for (int u = cluster; ok && u < num_units; u += num_clusters) {
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!__all_sync(0xffffffffu, mbar_wait(&bars->full[stage], phase))) { ok = false; break; }
-        // Consecutive lanes take consecutive 16-byte chunks: each quarter
-        // warp covers one 128-byte row, all 32 banks.
-        const uint32_t raw = smem_u32(stage_base + stage * kStageBytes) + t * 16;
+        const uint32_t a_raw = smem_u32(stage_base + stage * kStageBytes);
+        const uint32_t b_raw = a_raw + kTileBytes;
+        const uint32_t a_pk = a_raw + kRawBytes;
+        const uint32_t b_pk = b_raw + kRawBytes;
+        // Work unit: 8 consecutive fp32 of one row (32 bytes in, 2 x 16
+        // bytes of bf16 out); 512 per operand per stage, 2 per thread. The
+        // unit order makes each quarter warp touch 8 distinct 16-byte bank
+        // groups on every access.
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint4 v[kSplitChunks / 2];
+        for (int i = 0; i < kUnitsPerThread; ++i) {
+          // A (K-major rows of 128 bytes): row r, 8-deep K group g = raw
+          // 16-byte chunks 2g, 2g+1 (128-byte swizzle: chunk c of row r at
+          // c ^ (r & 7)). Packed row: [lo(8) | hi(8)] per group.
+          const int u = i * kSplitThreads + t;
+          const int r = u >> 2, g = u & 3, sw = r & 7;
+          const uint32_t c0 = r * 128 + ((2 * g) ^ sw) * 16, c1 = r * 128 + ((2 * g + 1) ^ sw) * 16;
+          uint4 hi, lo;
+          split8_bf16(lds128(a_raw + c0), lds128(a_raw + c1), hi, lo);
+          sts128(a_pk + c0, lo);
+          sts128(a_pk + c1, hi);
+        }
 #pragma unroll
-          for (int i = 0; i < kSplitChunks / 2; ++i)
-            v[i] = lds128(raw + (half * (kSplitChunks / 2) + i) * kSplitThreads * 16);
-#pragma unroll
-          for (int i = 0; i < kSplitChunks / 2; ++i)
-            sts128(raw + kRawBytes + (half * (kSplitChunks / 2) + i) * kSplitThreads * 16,
-                   make_uint4(tf32_lo(v[i].x), tf32_lo(v[i].y), tf32_lo(v[i].z),
-                              tf32_lo(v[i].w)));
+        for (int i = 0; i < kUnitsPerThread; ++i) {
+          const int u = i * kSplitThreads + t;
+          uint4 hi, lo;
+          if (b_kn) {
+            // B stored [K][N]: raw 32-column blocks j of 32 K-rows x 128
+            // bytes (32-byte chunk q of row k at q ^ (k & 3)). Packed: 64-
+            // column blocks jb of 64 K'-rows x 128 bytes (16-byte chunk c of
+            // row k' at c ^ (k' & 7)); for K group g, rows 16g..16g+7 hold
+            // hi, rows 16g+8..16g+15 lo.
+            const int q = u & 3, jodd = (u >> 2) & 1, k = (u >> 3) & 31, jb = u >> 8;
+            const uint32_t src = b_raw + (2 * jb + jodd) * 4096 + k * 128 + ((q ^ (k & 3)) * 32);
+            const uint32_t o0 = jodd * 16;  // odd blocks read their halves in swapped order
+            const uint4 pa = lds128(src + o0), pb = lds128(src + (16 - o0));
+            split8_bf16(jodd ? pb : pa, jodd ? pa : pb, hi, lo);
+            const int kr = k & 7;
+            const uint32_t dst = b_pk + jb * 8192 + (16 * (k >> 3) + kr) * 128 +
+                                 (((jodd * 4 + q) ^ kr) * 16);
+            sts128(dst, hi);
+            sts128(dst + 8 * 128, lo);
+          } else {
+            // B stored [N][K]: as A, packed row [hi(8) | lo(8)] per group.
+            const int r = u >> 2, g = u & 3, sw = r & 7;
+            const uint32_t c0 = r * 128 + ((2 * g) ^ sw) * 16;
+            const uint32_t c1 = r * 128 + ((2 * g + 1) ^ sw) * 16;
+            split8_bf16(lds128(b_raw + c0), lds128(b_raw + c1), hi, lo);
+            sts128(b_pk + c0, hi);
+            sts128(b_pk + c1, lo);
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -460,9 +536,11 @@ cudaError_t launch_gemm_f32_tcgen05(const GemmArgs &g, cudaStream_t stream) {
   const int num_units = split ? num_full + 2 * tail : pair_tiles;
   const uint32_t idesc_full = idesc_tf32_f32(2 * BM, BN, false, g.b_kn);
   const uint32_t idesc_half = idesc_tf32_f32(2 * BM, BN / 2, false, g.b_kn);
+  const uint32_t idesc16_full = idesc_f16_f32(2 * BM, BN, true, false, g.b_kn);
+  const uint32_t idesc16_half = idesc_f16_f32(2 * BM, BN / 2, true, false, g.b_kn);
   gemm_f32_pair_kernel<<<2 * clusters, kThreads, kSmemBytes, stream>>>(
       cache.a, cache.b, cache.d, g.Cin, g.ldc, g.M, g.N, g.K, idesc_full, idesc_half,
-      g.b_kn ? 1 : 0, num_full, num_units,
+      idesc16_full, idesc16_half, g.b_kn ? 1 : 0, num_full, num_units,
       (size_t)g.K * (size_t)g.N * 4 > kGroupAboveBBytes ? kGroupRows : 1, kChunkK / BK);
   return cudaGetLastError();
 }
