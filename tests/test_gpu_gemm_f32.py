@@ -155,3 +155,17 @@ def test_gemm_f32_grouped_tile_order_large_b(gpu, dev, orc):
     in groups of 8 pair rows; M = 2304 is 9 pair rows (a partial last group)."""
     _run(gpu, dev, orc, 2304, 4096, 4608, True, seed=77, rows=(2240, 2304))
     _run(gpu, dev, orc, 2304, 4096, 4608, False, seed=78, rows=(0, 48))
+
+
+def test_gemm_f32_rejects_bad_shapes(gpu, dev):
+    d = dev.alloc(4096)
+    F32 = gpu.Dtype.F32
+    assert gpu.gemm(d.ptr, d.ptr, d.ptr, None, 0, 8, 8, 8, 8, 8, 0, F32) == gpu.VCError.InvalidValue
+    # lda < K
+    assert gpu.gemm(d.ptr, d.ptr, d.ptr, None, 8, 8, 8, 4, 8, 8, 0, F32) == gpu.VCError.InvalidValue
+    # 64 x 64 fp32 operands need 16 KiB each: refused before launch, while
+    # 32 x 32 (4 KiB each) fits.
+    assert gpu.gemm(d.ptr, d.ptr, d.ptr, None, 64, 64, 64, 64, 64, 64, 0, F32) == gpu.VCError.InvalidValue
+    a, b, c = dev.alloc(4096), dev.alloc(4096), dev.alloc(4096)
+    assert gpu.gemm(a.ptr, b.ptr, c.ptr, None, 32, 32, 32, 32, 32, 32, 0, F32) == 0
+    assert gpu.vcDeviceSynchronize() == 0
