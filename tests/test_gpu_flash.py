@@ -69,8 +69,11 @@ def test_flash_attn_legacy_constants(gpu, dev, orc):
 @pytest.mark.parametrize("BH,N,d,causal", [(1, 256, 64, False), (2, 100, 16, True),
                                            (3, 333, 128, False), (2, 64, 32, True),
                                            (2, 97, 24, True), (1, 130, 48, False),
-                                           (1, 64, 100, True), (3, 40, 8, False)])
+                                           (1, 64, 100, True), (3, 40, 8, False),
+                                           (2, 77, 17, True), (1, 50, 3, False)])
 def test_flash_f32_vs_oracle(gpu, dev, orc, BH, N, d, causal):
+    """d % 4 != 0 (17, 3) stages K / V with 4-byte copies, the rest with
+    16-byte copies."""
     rng = np.random.default_rng(BH * N + d)
     Q, K, V = (rng.standard_normal(BH * N * d).astype(np.float32) for _ in range(3))
     s = np.float32(LOG2E / math.sqrt(d))
@@ -78,6 +81,24 @@ def test_flash_f32_vs_oracle(gpu, dev, orc, BH, N, d, causal):
     assert gpu.flash_fwd(dq.ptr, dk.ptr, dv.ptr, do.ptr, BH, N, d, s, causal, gpu.Dtype.F32) == 0
     assert gpu.vcDeviceSynchronize() == 0
     ref = orc.attention(Q, K, V, BH, N, d, s, causal)
+    assert np.abs(do.to_host(np.float32, Q.size) - ref).max() <= TOL["f32"]
+
+
+def test_flash_f32_unaligned_kv_pointers(gpu, dev, orc):
+    """K and V starting 4 bytes past a 16-byte boundary take the 4-byte
+    staging path with the same result."""
+    BH, N, d = 2, 90, 32
+    rng = np.random.default_rng(5)
+    Q, K, V = (rng.standard_normal(BH * N * d).astype(np.float32) for _ in range(3))
+    s = np.float32(LOG2E / math.sqrt(d))
+    pad = np.zeros(1, np.float32)
+    dq = dev.put(Q)
+    dk, dv = dev.put(np.concatenate([pad, K])), dev.put(np.concatenate([pad, V]))
+    do = dev.alloc(Q.nbytes)
+    assert gpu.flash_fwd(dq.ptr, dk.ptr + 4, dv.ptr + 4, do.ptr, BH, N, d, s, True,
+                         gpu.Dtype.F32) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    ref = orc.attention(Q, K, V, BH, N, d, s, True)
     assert np.abs(do.to_host(np.float32, Q.size) - ref).max() <= TOL["f32"]
 
 

@@ -10,8 +10,12 @@
 //   m = max(m_a, m_b), l = l_a 2^(m_a-m) + l_b 2^(m_b-m), acc likewise.
 // Any head dimension d <= 128. K/V tiles (64 keys; 32 at d > 64, halving the
 // shared memory) stream through a ring of kStages shared-memory buffers
-// filled by cp.async, so the loads of the next tiles overlap the arithmetic
-// on the current one. Small grids (the 1 x 256 x 64 demo shape is 16.8
+// filled by cp.async (16-byte copies when d % 4 == 0 and the rows are 16-byte
+// aligned, else 4-byte), so the loads of the next tiles overlap the
+// arithmetic on the current one. Rows are padded to d + 4 floats: lanes that
+// read 16 bytes of different keys' rows at the same column then fall on
+// distinct banks within every quarter warp, and each dot product runs as
+// four independent FMA chains over float4 reads. Small grids (the 1 x 256 x 64 demo shape is 16.8
 // MFLOP, latency-bound) run 4 rows of 32 lanes per block, for more blocks,
 // with a 4-deep ring (all of a 256-key sequence in flight at once); grids
 // that fill the GPU run 8 rows of 16 lanes, so that each staged K/V element
@@ -43,14 +47,21 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+__device__ __forceinline__ void cp_async16(float *smem_dst, const float *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(src)
+               : "memory");
+}
+
 // Shared memory: Q rows, then kStages K buffers and kStages V buffers of
-// kKeyTile keys; rows padded to D + 1 floats so that the lanes reading
-// different keys of one column hit different banks.
+// kKeyTile keys; rows padded to D + 4 floats (16-byte aligned rows whose
+// 16-byte columns spread over the banks, see above).
 template <int D, int kRows, int kLanes, int kStages>
 struct F32Smem {
   static constexpr int kKeyTile = D > 64 ? 32 : 64;
   static constexpr int kThreads = kRows * kLanes;
-  static constexpr int kPitch = D + 1;
+  static constexpr int kPitch = D + 4;
   static constexpr size_t kQ = 0;
   static constexpr size_t kK = kQ + size_t(kRows) * kPitch;
   static constexpr size_t kV = kK + kStages * size_t(kKeyTile) * kPitch;
@@ -64,7 +75,7 @@ template <int D, int kRows, int kLanes, int kStages>
 __global__ void __launch_bounds__(kRows * kLanes)
 flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
                  const float *__restrict__ V, float *__restrict__ O, int N, int d,
-                 float scale_log2, int causal) {
+                 float scale_log2, int causal, int vec16) {
   using L = F32Smem<D, kRows, kLanes, kStages>;
   constexpr int kKeyTile = L::kKeyTile, kThreads = L::kThreads;
   extern __shared__ float fsm[];
@@ -85,16 +96,32 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
     float *Kb = fsm + L::kK + size_t(b) * kKeyTile * L::kPitch;
     float *Vb = fsm + L::kV + size_t(b) * kKeyTile * L::kPitch;
     const int k0 = t * kKeyTile;
-    for (int i = threadIdx.x; i < kKeyTile * D; i += kThreads) {
-      const int rr = i / D, dd = i % D;
-      float *kd = Kb + rr * L::kPitch + dd, *vd = Vb + rr * L::kPitch + dd;
-      if (k0 + rr < N && dd < d) {
-        const int64_t off = base + static_cast<int64_t>(k0 + rr) * d + dd;
-        cp_async4(kd, K + off);
-        cp_async4(vd, V + off);
-      } else {
-        *kd = 0.0f;
-        *vd = 0.0f;
+    if (vec16) {
+      // d % 4 == 0: a 4-float group is wholly inside or outside the row.
+      for (int i = threadIdx.x; i < kKeyTile * (D / 4); i += kThreads) {
+        const int rr = i / (D / 4), dd = (i % (D / 4)) * 4;
+        float *kd = Kb + rr * L::kPitch + dd, *vd = Vb + rr * L::kPitch + dd;
+        if (k0 + rr < N && dd < d) {
+          const int64_t off = base + static_cast<int64_t>(k0 + rr) * d + dd;
+          cp_async16(kd, K + off);
+          cp_async16(vd, V + off);
+        } else {
+          *reinterpret_cast<float4 *>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4 *>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    } else {
+      for (int i = threadIdx.x; i < kKeyTile * D; i += kThreads) {
+        const int rr = i / D, dd = i % D;
+        float *kd = Kb + rr * L::kPitch + dd, *vd = Vb + rr * L::kPitch + dd;
+        if (k0 + rr < N && dd < d) {
+          const int64_t off = base + static_cast<int64_t>(k0 + rr) * d + dd;
+          cp_async4(kd, K + off);
+          cp_async4(vd, V + off);
+        } else {
+          *kd = 0.0f;
+          *vd = 0.0f;
+        }
       }
     }
     cp_async_commit();
@@ -128,11 +155,18 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
       const int jj = lane + h * kLanes;
       const int j = t * kKeyTile + jj;
       if (j >= N || (causal && j > qi)) continue;
-      const float *krow = Kb + jj * L::kPitch;
-      float dot = 0.0f;
+      const float4 *k4 = reinterpret_cast<const float4 *>(Kb + jj * L::kPitch);
+      const float4 *q4 = reinterpret_cast<const float4 *>(qrow);
+      float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
 #pragma unroll
-      for (int dd = 0; dd < D; ++dd) dot = fmaf(qrow[dd], krow[dd], dot);
-      const float s = dot * scale_log2;
+      for (int c = 0; c < D / 4; ++c) {
+        const float4 qv = q4[c], kv = k4[c];
+        d0 = fmaf(qv.x, kv.x, d0);
+        d1 = fmaf(qv.y, kv.y, d1);
+        d2 = fmaf(qv.z, kv.z, d2);
+        d3 = fmaf(qv.w, kv.w, d3);
+      }
+      const float s = ((d0 + d1) + (d2 + d3)) * scale_log2;
       if (s > m) {
         const float alpha = exp2f(m - s);  // 0 when m = -inf
         l *= alpha;
@@ -142,9 +176,15 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
       }
       const float p = exp2f(s - m);
       l += p;
-      const float *vrow = Vb + jj * L::kPitch;
+      const float4 *v4 = reinterpret_cast<const float4 *>(Vb + jj * L::kPitch);
 #pragma unroll
-      for (int dd = 0; dd < D; ++dd) acc[dd] = fmaf(p, vrow[dd], acc[dd]);
+      for (int c = 0; c < D / 4; ++c) {
+        const float4 vv = v4[c];
+        acc[4 * c] = fmaf(p, vv.x, acc[4 * c]);
+        acc[4 * c + 1] = fmaf(p, vv.y, acc[4 * c + 1]);
+        acc[4 * c + 2] = fmaf(p, vv.z, acc[4 * c + 2]);
+        acc[4 * c + 3] = fmaf(p, vv.w, acc[4 * c + 3]);
+      }
     }
     __syncthreads();  // buffer t % kStages is refilled by the stage() of iteration t + 1
   }
@@ -190,10 +230,12 @@ cudaError_t launch_dr(const FlashArgs &f, cudaStream_t stream) {
     }
   }
   dim3 grid((f.N + kRows - 1) / kRows, f.BH);
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const int vec16 = (f.d % 4 == 0 && al16(f.K) && al16(f.V)) ? 1 : 0;
   flash_f32_kernel<D, kRows, kLanes, kStages><<<grid, L::kThreads, L::kBytes, stream>>>(
       static_cast<const float *>(f.Q), static_cast<const float *>(f.K),
       static_cast<const float *>(f.V), static_cast<float *>(f.O), f.N, f.d, f.scale_log2,
-      f.causal ? 1 : 0);
+      f.causal ? 1 : 0, vec16);
   return cudaGetLastError();
 }
 
