@@ -33,7 +33,10 @@
 // cycles per N = 256 MMA with A and B from shared memory (a back-to-back
 // probe gives 166-173, the same for cta_group::1 and ::2, any operand
 // layout); the epilogue (~5K cycles per tile) is hidden by the second
-// accumulator. With A in TMEM the MMA alone costs 138-140 cycles, but
+// accumulator. The pair kernel is launched with programmatic stream
+// serialization, so back-to-back GEMMs overlap the next launch and its set-up
+// with the current one's last wave (400 back-to-back 4096^3 launches: 112.4
+// -> 110.3 us each). With A in TMEM the MMA alone costs 138-140 cycles, but
 // copying each K = 16 slice of A there (tcgen05.cp into 32 columns of the
 // drained accumulator, then the TS form) made this kernel 25-35 % slower
 // (4096^3: 776 vs 1197 TFLOP/s), so A stays in shared memory.
@@ -371,6 +374,12 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   cluster_sync();  // barriers of both CTAs initialised before any cross-CTA use
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // Launched with programmatic stream serialization: the next launch may be
+  // scheduled from here on (its blocks take an SM as this grid's leave it and
+  // set up there), and this grid touches global memory only once the previous
+  // one has completed.
+  grid_launch_dependents();
+  grid_dependency_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -621,11 +630,23 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
     const int num_units = split ? num_full + 2 * tail : pair_tiles;
     const uint32_t idesc_full = idesc_f16_f32(2 * BM, BN, g.bf16, false, g.b_kn);
     const uint32_t idesc_half = idesc_f16_f32(2 * BM, BN / 2, g.bf16, false, g.b_kn);
-    gemm_tcgen05_pair_kernel<<<2 * clusters, kThreads, kPairSmemBytes, stream>>>(
-        cache.a, cache.b_pair, cache.d, g.Cin, g.ldc, g.M, g.N, g.K, idesc_full, idesc_half,
-        g.b_kn ? 1 : 0, num_full, num_units,
-        (size_t)g.K * (size_t)g.N * 2 > kGroupAboveBBytes ? kGroupRows : 1);
-    return cudaGetLastError();
+    // Programmatic stream serialization: back-to-back launches overlap the
+    // next one's launch and set-up with this one's last wave (the kernel
+    // waits for the previous grid before touching global memory).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_tcgen05_pair_kernel, cache.a, cache.b_pair, cache.d,
+                              g.Cin, g.ldc, g.M, g.N, g.K, idesc_full, idesc_half,
+                              g.b_kn ? 1 : 0, num_full, num_units,
+                              (size_t)g.K * (size_t)g.N * 2 > kGroupAboveBBytes ? kGroupRows : 1);
   }
   const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
   const int grid = tiles < sms ? tiles : sms;

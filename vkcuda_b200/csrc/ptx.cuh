@@ -137,6 +137,18 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
                : "memory");
 }
 
+// Programmatic dependent launch. grid_dependency_wait(): block until the
+// grids this launch depends on have completed and their writes are visible
+// (returns at once when there is no such dependency). grid_launch_dependents():
+// let the next launch in the stream be scheduled now, before this grid ends;
+// its blocks still wait in grid_dependency_wait() for this grid to finish.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map))
