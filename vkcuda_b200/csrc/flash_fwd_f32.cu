@@ -20,8 +20,13 @@
 // with a 4-deep ring (all of a 256-key sequence in flight at once); grids
 // that fill the GPU run 8 rows of 16 lanes, so that each staged K/V element
 // serves twice the rows in a block of the same 128 threads, with a 2-deep
-// ring so that several blocks share an SM. exp2f is the accurate CUDA function, so
-// the result tracks an fp64 evaluation to ~1e-6 for unit-variance inputs.
+// ring so that several blocks share an SM. A lane rescales its running state
+// once per key tile (to the tile's maximum), and the lanes of a row merge
+// their states at the end through shared memory: each lane rescales its own
+// accumulators to the row maximum and writes them, then sums a column per
+// output element (a shuffle butterfly over the 64-wide accumulators took a
+// fifth of the kernel's instructions). exp2f is the accurate CUDA function,
+// so the result tracks an fp64 evaluation to ~1e-6 for unit-variance inputs.
 #include <cuda_runtime.h>
 #include <cmath>
 #include <cstdint>
@@ -130,6 +135,15 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
   float m = -INFINITY, l = 0.0f, acc[D];
 #pragma unroll
   for (int dd = 0; dd < D; ++dd) acc[dd] = 0.0f;
+  // Up to d = 64 the query row also lives in registers (beside the 64
+  // accumulators); wider rows are read from shared memory.
+  constexpr bool kQInRegs = D <= 64;
+  constexpr int kH = kKeyTile / kLanes;  // keys of a tile per lane
+  // Merge area per row, +16 floats so that the two rows of a warp (16 lanes
+  // each) fall on opposite halves of the banks.
+  constexpr int kMergeRowStride = D * (kLanes + 1) + 16;
+  static_assert(size_t(kRows) * kMergeRowStride <= L::kFloats, "merge area fits");
+  float4 qreg[kQInRegs ? D / 4 : 1];
 
   const int kend = causal ? min(N, q0 + kRows) : N;
   const int ntiles = (kend + kKeyTile - 1) / kKeyTile;
@@ -150,31 +164,47 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
     const float *Kb = fsm + L::kK + size_t(t % kStages) * kKeyTile * L::kPitch;
     const float *Vb = fsm + L::kV + size_t(t % kStages) * kKeyTile * L::kPitch;
     const float *qrow = Qs + r * L::kPitch;
+    if (kQInRegs && t == 0) {
 #pragma unroll
-    for (int h = 0; h < kKeyTile / kLanes; ++h) {
+      for (int c = 0; c < (kQInRegs ? D / 4 : 1); ++c)
+        qreg[c] = reinterpret_cast<const float4 *>(qrow)[c];
+    }
+    // Scores of this lane's keys of the tile first, then one rescale of the
+    // running state to the tile's maximum, then the probabilities.
+    float sc[kH];
+    float mt = m;
+#pragma unroll
+    for (int h = 0; h < kH; ++h) {
       const int jj = lane + h * kLanes;
       const int j = t * kKeyTile + jj;
-      if (j >= N || (causal && j > qi)) continue;
       const float4 *k4 = reinterpret_cast<const float4 *>(Kb + jj * L::kPitch);
       const float4 *q4 = reinterpret_cast<const float4 *>(qrow);
       float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
 #pragma unroll
       for (int c = 0; c < D / 4; ++c) {
-        const float4 qv = q4[c], kv = k4[c];
+        const float4 qv = kQInRegs ? qreg[kQInRegs ? c : 0] : q4[c];
+        const float4 kv = k4[c];
         d0 = fmaf(qv.x, kv.x, d0);
         d1 = fmaf(qv.y, kv.y, d1);
         d2 = fmaf(qv.z, kv.z, d2);
         d3 = fmaf(qv.w, kv.w, d3);
       }
-      const float s = ((d0 + d1) + (d2 + d3)) * scale_log2;
-      if (s > m) {
-        const float alpha = exp2f(m - s);  // 0 when m = -inf
-        l *= alpha;
+      const bool valid = j < N && !(causal && j > qi);
+      sc[h] = valid ? ((d0 + d1) + (d2 + d3)) * scale_log2 : -INFINITY;
+      mt = fmaxf(mt, sc[h]);
+    }
+    if (mt > m) {
+      const float alpha = exp2f(m - mt);  // 0 when m = -inf
+      l *= alpha;
 #pragma unroll
-        for (int dd = 0; dd < D; ++dd) acc[dd] *= alpha;
-        m = s;
-      }
-      const float p = exp2f(s - m);
+      for (int dd = 0; dd < D; ++dd) acc[dd] *= alpha;
+      m = mt;
+    }
+#pragma unroll
+    for (int h = 0; h < kH; ++h) {
+      if (sc[h] == -INFINITY) continue;  // masked or past the end
+      const int jj = lane + h * kLanes;
+      const float p = exp2f(sc[h] - m);
       l += p;
       const float4 *v4 = reinterpret_cast<const float4 *>(Vb + jj * L::kPitch);
 #pragma unroll
@@ -188,27 +218,37 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
     }
     __syncthreads();  // buffer t % kStages is refilled by the stage() of iteration t + 1
   }
-  // Merge the kLanes lane states of the row (consecutive lanes of a warp).
+  // Merge the row's kLanes lane states (consecutive lanes of one warp): the
+  // row maximum and the rescaled sum by shuffles, the rescaled accumulators
+  // through shared memory (all of it is free once the last tile's trailing
+  // barrier has passed), [D][kLanes + 1] per row so that both the writes and
+  // the column sums below touch 32 distinct banks; each lane then sums the
+  // output columns dd = lane (mod kLanes).
+  float mrow = m;
 #pragma unroll
-  for (int off = kLanes / 2; off > 0; off >>= 1) {
-    const float m_o = __shfl_xor_sync(0xffffffffu, m, off);
-    const float l_o = __shfl_xor_sync(0xffffffffu, l, off);
-    const float mn = fmaxf(m, m_o);
-    const float a = (m == -INFINITY) ? 0.0f : exp2f(m - mn);
-    const float b = (m_o == -INFINITY) ? 0.0f : exp2f(m_o - mn);
-    l = l * a + l_o * b;
+  for (int off = kLanes / 2; off > 0; off >>= 1)
+    mrow = fmaxf(mrow, __shfl_xor_sync(0xffffffffu, mrow, off));
+  const float own = (m == -INFINITY) ? 0.0f : exp2f(m - mrow);
+  float lrow = l * own;
 #pragma unroll
-    for (int dd = 0; dd < D; ++dd) {
-      const float acc_o = __shfl_xor_sync(0xffffffffu, acc[dd], off);
-      acc[dd] = acc[dd] * a + acc_o * b;
-    }
-    m = mn;
-  }
+  for (int off = kLanes / 2; off > 0; off >>= 1)
+    lrow += __shfl_xor_sync(0xffffffffu, lrow, off);
+  float *part = fsm + size_t(r) * kMergeRowStride;
+#pragma unroll
+  for (int dd = 0; dd < D; ++dd) part[dd * (kLanes + 1) + lane] = acc[dd] * own;
+  __syncwarp();
   if (qi < N) {
-    const float inv = 1.0f / l;
+    const float inv = 1.0f / lrow;
+    for (int dd = lane; dd < d; dd += kLanes) {
+      const float *col = part + dd * (kLanes + 1);
+      float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
-    for (int dd = 0; dd < D; ++dd)
-      if (dd % kLanes == lane && dd < d) O[base + static_cast<int64_t>(qi) * d + dd] = acc[dd] * inv;
+      for (int j = 0; j < kLanes; j += 2) {
+        s0 += col[j];
+        s1 += col[j + 1];
+      }
+      O[base + static_cast<int64_t>(qi) * d + dd] = (s0 + s1) * inv;
+    }
   }
 }
 
