@@ -79,7 +79,9 @@ constexpr int kWgThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kBoxBytes = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-constexpr int kCausalGroup = 8;            // slices per causal ordering group
+// Slices per causal ordering group (8 x 16 x 4096 x 128: groups of 4 / 8 /
+// 16 ran 552 / 539 / 542 us; at N = 16384, 932 / 938 / 950 us).
+constexpr int kCausalGroup = 8;
 
 
 
