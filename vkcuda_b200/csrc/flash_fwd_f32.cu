@@ -218,25 +218,46 @@ flash_f32_kernel(const float *__restrict__ Q, const float *__restrict__ K,
     }
     __syncthreads();  // buffer t % kStages is refilled by the stage() of iteration t + 1
   }
-  // Merge the row's kLanes lane states (consecutive lanes of one warp): the
-  // row maximum and the rescaled sum by shuffles, the rescaled accumulators
-  // through shared memory (all of it is free once the last tile's trailing
-  // barrier has passed), [D][kLanes + 1] per row so that both the writes and
-  // the column sums below touch 32 distinct banks; each lane then sums the
-  // output columns dd = lane (mod kLanes).
+  // Merge the row's kLanes lane states (consecutive lanes: one warp, half a
+  // warp, or two warps for kLanes = 64): the row maximum and the rescaled sum
+  // by shuffles (and, across the two warps of a 64-lane row, through shared
+  // memory), the rescaled accumulators through shared memory (all of the
+  // dynamic area is free once the last tile's trailing barrier has passed),
+  // [D][kLanes + 1] per row so that both the writes and the column sums below
+  // touch 32 distinct banks; each lane then sums the output columns
+  // dd = lane (mod kLanes).
+  constexpr int kWarpLanes = kLanes < 32 ? kLanes : 32;
+  constexpr int kRowWarps = kLanes / kWarpLanes;
+  __shared__ float row_red[kRows][kRowWarps][2];
   float mrow = m;
 #pragma unroll
-  for (int off = kLanes / 2; off > 0; off >>= 1)
+  for (int off = kWarpLanes / 2; off > 0; off >>= 1)
     mrow = fmaxf(mrow, __shfl_xor_sync(0xffffffffu, mrow, off));
+  if (kRowWarps > 1) {
+    if ((lane & 31) == 0) row_red[r][lane >> 5][0] = mrow;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kRowWarps; ++w) mrow = fmaxf(mrow, row_red[r][w][0]);
+  }
   const float own = (m == -INFINITY) ? 0.0f : exp2f(m - mrow);
   float lrow = l * own;
 #pragma unroll
-  for (int off = kLanes / 2; off > 0; off >>= 1)
+  for (int off = kWarpLanes / 2; off > 0; off >>= 1)
     lrow += __shfl_xor_sync(0xffffffffu, lrow, off);
+  if (kRowWarps > 1) {
+    if ((lane & 31) == 0) row_red[r][lane >> 5][1] = lrow;
+  }
   float *part = fsm + size_t(r) * kMergeRowStride;
 #pragma unroll
   for (int dd = 0; dd < D; ++dd) part[dd * (kLanes + 1) + lane] = acc[dd] * own;
-  __syncwarp();
+  if (kRowWarps > 1) {
+    __syncthreads();
+    lrow = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kRowWarps; ++w) lrow += row_red[r][w][1];
+  } else {
+    __syncwarp();
+  }
   if (qi < N) {
     const float inv = 1.0f / lrow;
     for (int dd = lane; dd < d; dd += kLanes) {
@@ -292,8 +313,13 @@ cudaError_t launch_d(const FlashArgs &f, cudaStream_t stream) {
       sms = 148;
   }
   const long long blocks8 = (long long)f.BH * ((f.N + 7) / 8);
-  return blocks8 >= 2LL * sms ? launch_dr<D, 8, 16, 2>(f, stream)
-                              : launch_dr<D, 4, 32, 4>(f, stream);
+  if (blocks8 >= 2LL * sms) return launch_dr<D, 8, 16, 2>(f, stream);
+  // Grids too small to fill the GPU with 4-row blocks: up to d = 64, two
+  // rows of 64 lanes (two warps) per block halve the keys each lane walks.
+  if (D <= 64 && (long long)f.BH * ((f.N + 3) / 4) < sms) {
+    if constexpr (D <= 64) return launch_dr<D, 2, 64, 4>(f, stream);
+  }
+  return launch_dr<D, 4, 32, 4>(f, stream);
 }
 
 }  // namespace
