@@ -15,9 +15,12 @@
 // arithmetic on the current one. Rows are padded to d + 4 floats: lanes that
 // read 16 bytes of different keys' rows at the same column then fall on
 // distinct banks within every quarter warp, and each dot product runs as
-// four independent FMA chains over float4 reads. Small grids (the 1 x 256 x 64 demo shape is 16.8
-// MFLOP, latency-bound) run 4 rows of 32 lanes per block, for more blocks,
-// with a 4-deep ring (all of a 256-key sequence in flight at once); grids
+// four independent FMA chains over float4 reads. Small grids (the
+// 1 x 256 x 64 demo shape is 16.8 MFLOP, latency-bound) run 4 rows of 32
+// lanes per block, for more blocks, with a 4-deep ring (all of a 256-key
+// sequence in flight at once); grids that would not give every SM a 4-row
+// block run, up to d = 64, 2 rows of 64 lanes (two warps per row: each lane
+// walks half as many keys; 1 x 256 x 64: 8.5 -> 5.8 us per launch); grids
 // that fill the GPU run 8 rows of 16 lanes, so that each staged K/V element
 // serves twice the rows in a block of the same 128 threads, with a 2-deep
 // ring so that several blocks share an SM. A lane rescales its running state
