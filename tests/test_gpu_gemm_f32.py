@@ -81,6 +81,30 @@ def test_gemm_f32_random_vs_oracle(gpu, dev, orc, M, N, K, b_kn):
     _run(gpu, dev, orc, M, N, K, b_kn, seed=M * 7 + N * 3 + K + int(b_kn))
 
 
+@pytest.mark.parametrize("b_kn", [True, False])
+def test_gemm_f32_split_k_small_grid_deterministic(gpu, dev, orc, b_kn):
+    """1024 x 1024 x 1024 fills 16 of the GPU's SM pairs, so K is split in
+    two halves that both add onto a zeroed C: results within the bar, with
+    the addend, and identical on a second call."""
+    M = N = K = 1024
+    rng = np.random.default_rng(21 + int(b_kn))
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N) if b_kn else (N, K)).astype(np.float32)
+    cin = rng.standard_normal((M, N)).astype(np.float32)
+    dA, dB, dC, dD = dev.put(A), dev.put(B), dev.put(cin), dev.alloc(M * N * 4)
+    outs = []
+    for _ in range(2):
+        assert gpu.gemm(dA.ptr, dB.ptr, dD.ptr, dC.ptr, M, N, K, K, N if b_kn else K, N, N,
+                        gpu.Dtype.F32, b_kn) == 0
+        assert gpu.vcDeviceSynchronize() == 0
+        outs.append(dD.to_host(np.float32, M * N).reshape(M, N))
+    assert np.array_equal(outs[0], outs[1])
+    ldb = N if b_kn else K
+    ref = orc.gemm(A, B, M, N, K, K, ldb, b_kn, Cin=cin, ldc=N)
+    mag = orc.gemm(np.abs(A), np.abs(B), M, N, K, K, ldb, b_kn)
+    assert (np.abs(outs[0].astype(np.float64) - ref) <= BOUND * mag + 1e-6).all()
+
+
 def test_gemm_f32_with_addend_and_strides(gpu, dev, orc):
     _run(gpu, dev, orc, 200, 300, 256, True, lda=260, ldb=304, ldd=308, with_c=True, seed=5)
     _run(gpu, dev, orc, 200, 300, 256, False, lda=260, ldb=264, ldd=300, with_c=True, seed=6)

@@ -47,6 +47,10 @@
 //                rest.
 // B stored [K][N] (the demos' layout) is an MN-major operand; for tf32 that
 // takes the 128-byte swizzle with 32-byte atoms, in TMA and descriptor.
+// Grids that would fill at most half the SM pairs (the demos' sizes) with
+// K <= 1024 split K in two: both halves reduce-add onto a C zeroed on the
+// stream first, two round-to-nearest adds onto zero per element, so the
+// result does not depend on their order (1024^3: 43.2 -> 30.9 us).
 // Shared memory per stage: A raw, B raw, A packed, B packed = 64 KiB; 3
 // stages + 32 KiB of epilogue staging = 224 KiB. Ragged M, N, K: TMA
 // zero-fills loads outside the matrix and clips stores. Roofline: per
@@ -167,7 +171,7 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                      const float *__restrict__ Cin, int64_t ldc, int M, int N, int K,
                      uint32_t idesc_full, uint32_t idesc_half, uint32_t idesc16_full,
                      uint32_t idesc16_half, int b_kn, int num_full, int num_units,
-                     int group_rows, int chunk_kblocks) {
+                     int group_rows, int chunk_kblocks, int split_k) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -185,15 +189,23 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   const int kblocks = (K + BK - 1) / BK;
   // Unit -> tile as in the fp16 pair kernel: full 256 x 256 tiles, then the
   // tail wave's tiles as 256 x 128 halves; groups of `group_rows` pair rows
-  // walked column by column.
-  auto unit_tile = [&](int u, int &tm, int &n0, int &width) {
-    int tile = u, half = 0;
+  // walked column by column. With split_k = 2 (grids that would fill at most
+  // half the clusters), unit u is the K part u % 2 of tile u / 2 instead,
+  // and [kb_begin, kb_end) its K blocks.
+  auto unit_tile = [&](int u, int &tm, int &n0, int &width, int &kb_begin, int &kb_end) {
+    int tile = u, half = 0, part = 0;
     width = BN;
-    if (u >= num_full) {
+    if (split_k > 1) {
+      tile = u / split_k;
+      part = u % split_k;
+    } else if (u >= num_full) {
       tile = num_full + (u - num_full) / 2;
       half = (u - num_full) & 1;
       width = BN / 2;
     }
+    const int per = (kblocks + split_k - 1) / split_k;
+    kb_begin = part * per;
+    kb_end = min(kblocks, kb_begin + per);
     const int group = tile / (group_rows * tiles_n);
     const int first_m = group * group_rows;
     const int rows = min(tiles_m - first_m, group_rows);
@@ -236,11 +248,11 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
       uint32_t issued = 0;
       bool ok = true;
       for (int u = cluster; ok && u < num_units; u += num_clusters) {
-        int tm, n0, width;
-        unit_tile(u, tm, n0, width);
+        int tm, n0, width, kb_begin, kb_end;
+        unit_tile(u, tm, n0, width, kb_begin, kb_end);
         const int a_row = tm * 2 * BM + rank * BM;
         const int b_col = n0 + rank * (width / 2);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1u)) { ok = false; break; }
           uint8_t *sA = stage_base + stage * kStageBytes;
           uint8_t *sB = sA + kTileBytes;
@@ -274,7 +286,9 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
       int local = 0;
       // One accumulator per (unit, K chunk), alternating between the two.
       for (int u = cluster; ok && u < num_units; u += num_clusters) {
-       for (int kb0 = 0; ok && kb0 < kblocks; kb0 += chunk_kblocks, ++local) {
+       int tm, n0, width, kb_begin, kb_end_unit;
+       unit_tile(u, tm, n0, width, kb_begin, kb_end_unit);
+       for (int kb0 = kb_begin; ok && kb0 < kb_end_unit; kb0 += chunk_kblocks, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         const uint32_t idesc = (u < num_full) ? idesc_full : idesc_half;
@@ -282,7 +296,7 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kAccCols;
-        const int kb_end = min(kblocks, kb0 + chunk_kblocks);
+        const int kb_end = min(kb_end_unit, kb0 + chunk_kblocks);
         for (int kb = kb0; kb < kb_end; ++kb) {
           // Cluster-scope acquire: the other CTA's split writes (fenced to
           // the tensor proxy before its release arrive) precede these MMAs.
@@ -328,7 +342,9 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     uint32_t phase = 0;
     bool ok = true;
     for (int u = cluster; ok && u < num_units; u += num_clusters) {
-      for (int kb = 0; kb < kblocks; ++kb) {
+      int tm, n0, width, kb_begin, kb_end;
+      unit_tile(u, tm, n0, width, kb_begin, kb_end);
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
         if (!__all_sync(0xffffffffu, mbar_wait(&bars->full[stage], phase))) { ok = false; break; }
         const uint32_t a_raw = smem_u32(stage_base + stage * kStageBytes);
         const uint32_t b_raw = a_raw + kTileBytes;
@@ -401,19 +417,22 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     uint32_t box_count = 0;
     bool ok = true;
     for (int u = cluster; ok && u < num_units; u += num_clusters) {
-      int tm, n0, width;
-      unit_tile(u, tm, n0, width);
+      int tm, n0, width, kb_begin, kb_end;
+      unit_tile(u, tm, n0, width, kb_begin, kb_end);
       const int m0 = tm * 2 * BM + rank * BM;
       const int gr = m0 + row;
       const int nboxes = width / kEpiCols;
-      for (int kb0 = 0; kb0 < kblocks; kb0 += chunk_kblocks, ++local) {
+      for (int kb0 = kb_begin; kb0 < kb_end; kb0 += chunk_kblocks, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&bars->acc_full[acc], acc_phase)) { ok = false; break; }
         tc_fence_after();
-        const bool first = kb0 == 0;
-        // A later K chunk adds onto what this warp stored for the earlier
-        // ones: those writes must have completed first.
+        const bool first = kb0 == kb_begin;
+        // The first chunk of an unsplit tile is stored; every other chunk is
+        // added onto C (a split tile's parts both add onto the C the host
+        // zeroed). A later chunk adds onto what this warp wrote for the
+        // earlier ones: those writes must have completed first.
+        const bool store = first && split_k == 1;
         if (!first) {
           if (lane == 0) bulk_wait_group<0>();
           __syncwarp();
@@ -429,13 +448,13 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
           }
           const int cn0 = n0 + c * kEpiCols;
           if (cn0 >= N) continue;
-          if (first && Cin != nullptr && gr < M) {
+          if (kb0 == 0 && Cin != nullptr && gr < M) {
             const float *crow = Cin + (int64_t)gr * ldc;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (cn0 + j < N) v[j] = __float_as_uint(__uint_as_float(v[j]) + crow[cn0 + j]);
           }
-          epilogue_store_box(&tmD, warp_stage, v, lane, box_count, cn0, m0 + quad * 32, !first);
+          epilogue_store_box(&tmD, warp_stage, v, lane, box_count, cn0, m0 + quad * 32, !store);
         }
       }
     }
@@ -529,11 +548,28 @@ cudaError_t launch_gemm_f32_tcgen05(const GemmArgs &g, cudaStream_t stream) {
   if (sms < 2) return cudaErrorNotSupported;
   const int pair_tiles = ((g.M + 2 * BM - 1) / (2 * BM)) * ((g.N + BN - 1) / BN);
   const int resident = clusters_resident(dev, sms);
-  const int clusters = pair_tiles < resident ? pair_tiles : resident;
-  const int tail = pair_tiles % clusters;
-  const bool split = tail > 0 && 2 * tail <= clusters;
-  const int num_full = split ? pair_tiles - tail : pair_tiles;
-  const int num_units = split ? num_full + 2 * tail : pair_tiles;
+  const int kblocks = (g.K + BK - 1) / BK;
+  constexpr int kChunkBlocks = kChunkK / BK;
+  // Split K in two when the tiles would fill at most half the clusters and
+  // each half is at most one K chunk: both halves add onto a zeroed C, so
+  // every element gets exactly two round-to-nearest adds onto zero and the
+  // result does not depend on their order.
+  const int split_k =
+      (2 * pair_tiles <= resident && kblocks >= 2 && kblocks <= 2 * kChunkBlocks) ? 2 : 1;
+  int clusters, num_full, num_units;
+  if (split_k == 2) {
+    num_full = num_units = 2 * pair_tiles;
+    clusters = num_units;
+    cudaError_t e = cudaMemset2DAsync(g.D, (size_t)g.ldd * sizeof(float), 0,
+                                      (size_t)g.N * sizeof(float), g.M, stream);
+    if (e != cudaSuccess) return e;
+  } else {
+    clusters = pair_tiles < resident ? pair_tiles : resident;
+    const int tail = pair_tiles % clusters;
+    const bool split = tail > 0 && 2 * tail <= clusters;
+    num_full = split ? pair_tiles - tail : pair_tiles;
+    num_units = split ? num_full + 2 * tail : pair_tiles;
+  }
   const uint32_t idesc_full = idesc_tf32_f32(2 * BM, BN, false, g.b_kn);
   const uint32_t idesc_half = idesc_tf32_f32(2 * BM, BN / 2, false, g.b_kn);
   const uint32_t idesc16_full = idesc_f16_f32(2 * BM, BN, true, false, g.b_kn);
@@ -541,7 +577,7 @@ cudaError_t launch_gemm_f32_tcgen05(const GemmArgs &g, cudaStream_t stream) {
   gemm_f32_pair_kernel<<<2 * clusters, kThreads, kSmemBytes, stream>>>(
       cache.a, cache.b, cache.d, g.Cin, g.ldc, g.M, g.N, g.K, idesc_full, idesc_half,
       idesc16_full, idesc16_half, g.b_kn ? 1 : 0, num_full, num_units,
-      (size_t)g.K * (size_t)g.N * 4 > kGroupAboveBBytes ? kGroupRows : 1, kChunkK / BK);
+      (size_t)g.K * (size_t)g.N * 4 > kGroupAboveBBytes ? kGroupRows : 1, kChunkBlocks, split_k);
   return cudaGetLastError();
 }
 
