@@ -134,6 +134,8 @@ int vc_graph_launch(void *graph, void *stream);      /* :616 */
 int vc_graph_reset(void *graph);                     /* :621 */
 int vc_load_kernel(const uint32_t *words, size_t wordCount,
                    const char *entryPoint, void **outKernel);           /* :625 */
+int vc_load_kernel_from_file(const char *path, const char *entryPoint,
+                             void **outKernel);                         /* :629 */
 int vc_release_kernel(void *kernel);                 /* vcReleaseKernel  :685 */
 int vc_launch_kernel(void *kernel, unsigned gridDim, unsigned blockDim,
                      const vc_kernel_arg *args, int argCount);          /* :699 */
@@ -227,7 +229,9 @@ int vc_block_reduce_f32(const float *in, float *out, int n, int block,
  * dtype VC_DTYPE_F32: A and B are fp32, computed on the tensor cores from a
  * hi/lo split of each operand (hi*hi in tf32, the two correction products in
  * bf16; at most ~2^-17 relative per product, rounded to nearest); replaces
- * matmulTiled (examples/matmul_bench.vc:22-54). */
+ * matmulTiled (examples/matmul_bench.vc:22-54).
+ * Cin may be D itself (in place, ldc == ldd); it must not otherwise overlap
+ * D, since one tile's stores may land on another tile's addend. */
 int vc_gemm(const void *A, const void *B, float *D, const float *Cin, int M,
             int N, int K, int64_t lda, int64_t ldb, int64_t ldd, int64_t ldc,
             int dtype, int b_kn, void *stream);

@@ -124,3 +124,18 @@ def half_bits_to_f32(bits: np.ndarray, bf16: bool) -> np.ndarray:
     import torch
     t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16))
     return t.view(torch.bfloat16 if bf16 else torch.float16).float().numpy()
+
+
+def spirv_module(entry: str) -> list:
+    """The words of a minimal SPIR-V module (header, Shader capability,
+    logical/GLSL450 memory model, one GLCompute OpEntryPoint named `entry`):
+    what vcLoadKernel is given by generated host code, reduced to the parts a
+    loader reads (SPIR-V 1.0 spec, section 2.3 physical layout)."""
+    name = entry.encode() + b"\0"
+    name += b"\0" * (-len(name) % 4)
+    name_words = [int.from_bytes(name[i:i + 4], "little") for i in range(0, len(name), 4)]
+    words = [0x07230203, 0x00010000, 0, 2, 0]          # magic, version 1.0, generator, bound, schema
+    words += [(2 << 16) | 17, 1]                         # OpCapability Shader
+    words += [(3 << 16) | 14, 0, 1]                      # OpMemoryModel Logical GLSL450
+    words += [((3 + len(name_words)) << 16) | 15, 5, 1] + name_words  # OpEntryPoint GLCompute %1
+    return words

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/ (run here, where the reference
 tree is mounted; the fixtures are committed and travel without it).
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference DIR]   (default: oracle.build_ref.reference_dir())
 
 Writes:
   fa_demo_causal0.bin, fa_demo_causal1.bin
@@ -67,11 +67,12 @@ def int_checksum(C: np.ndarray) -> dict:
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default="")
     args = ap.parse_args()
 
     from oracle import build_ref, oracle
 
+    args.reference = args.reference or build_ref.reference_dir()
     build_ref.build(args.reference, quiet=True)
     import torch
     import torch.nn.functional as F

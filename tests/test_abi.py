@@ -10,6 +10,8 @@ import sys
 
 import pytest
 
+from conftest import spirv_module
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -71,20 +73,47 @@ def test_no_device_behaviour(vc):
 
 def test_kernel_registry_host_logic(vc):
     for name in ["flashAttn", "wmma_gemm", "matmulCoopmat", "matmulTiled", "vadd", "blockReduce",
+                 "fillPattern",
                  "vc.gemm", "vc.flash_fwd", "vc.vadd", "vc.sum", "vc.vadd_sum",
                  "vc.block_reduce"]:
-        err, k = vc.vcLoadKernel(None, name)
+        err, k = vc.vcGetKernel(name)
         assert err == vc.VCError.Success and k, name
         assert vc.vcReleaseKernel(k) == vc.VCError.Success
-    # SPIR-V magic is checked when a module is given.
-    assert vc.vcLoadKernel([0x07230203, 0, 0], "vadd")[0] == vc.VCError.Success
-    assert vc.vcLoadKernel([0xdeadbeef], "vadd")[0] == vc.VCError.InvalidKernel
-    assert vc.vcLoadKernel(None, "noSuchKernel")[0] == vc.VCError.InvalidKernel
-    assert vc.vcLoadKernel([0x07230203, 1], "main")[0] == vc.VCError.InvalidKernel
-    err, k = vc.vcLoadKernel(None, "flashAttn")
+        # The reference-style load: a SPIR-V module whose entry names the kernel.
+        err, k = vc.vcLoadKernel(spirv_module(name), name)
+        assert err == vc.VCError.Success and k, name
+        assert vc.vcReleaseKernel(k) == vc.VCError.Success
+    # A missing module, one shorter than the 5-word header, or one without the
+    # SPIR-V magic is InvalidValue before the entry is looked at
+    # (reference lib/Runtime/VCRuntime.cpp:4261-4268).
+    assert vc.vcLoadKernel(None, "vadd")[0] == vc.VCError.InvalidValue
+    assert vc.vcLoadKernel([], "vadd")[0] == vc.VCError.InvalidValue
+    assert vc.vcLoadKernel([0x07230203, 0x00010000, 0, 1], "vadd")[0] == vc.VCError.InvalidValue
+    assert vc.vcLoadKernel([0xdeadbeef, 0x00010000, 0, 1, 0], "vadd")[0] == vc.VCError.InvalidValue
+    assert vc.vcLoadKernel([0x07230203, 0x00010000, 0, 1, 0], "vadd")[0] == vc.VCError.Success
+    # A well-formed module whose entry names no kernel here: InvalidKernel.
+    assert vc.vcLoadKernel(spirv_module("noSuchKernel"), "noSuchKernel")[0] == vc.VCError.InvalidKernel
+    assert vc.vcLoadKernel(spirv_module("main"), "main")[0] == vc.VCError.InvalidKernel
+    assert vc.vcGetKernel("noSuchKernel")[0] == vc.VCError.InvalidKernel
+    err, k = vc.vcGetKernel("flashAttn")
     assert vc.vcKernelSetConstant(k, "SEQ", 128) == vc.VCError.Success
     assert vc.vcKernelSetConstant(k, "NOPE", 1) == vc.VCError.InvalidValue
     assert vc.vcKernelSetConstant(k, "SEQ", 0) == vc.VCError.InvalidValue
+    vc.vcReleaseKernel(k)
+
+
+def test_load_kernel_from_file(vc, tmp_path):
+    # Whole words with the last one zero-padded, as the reference reads a file
+    # (VCRuntime.cpp:4378-4387): a 3-byte file is one word, too short.
+    import struct
+    short = tmp_path / "short.spv"
+    short.write_bytes(b"\x03\x02\x23")
+    assert vc.vcLoadKernelFromFile(str(short), "vadd")[0] == vc.VCError.InvalidValue
+    assert vc.vcLoadKernelFromFile(str(tmp_path / "absent.spv"), "vadd")[0] == vc.VCError.InvalidValue
+    good = tmp_path / "vadd.spv"
+    good.write_bytes(struct.pack(f"<{len(spirv_module('vadd'))}I", *spirv_module("vadd")))
+    err, k = vc.vcLoadKernelFromFile(str(good), "vadd")
+    assert err == vc.VCError.Success and k
     vc.vcReleaseKernel(k)
 
 
@@ -92,7 +121,7 @@ def test_launch_argument_checks(vc):
     # Null kernel -> InvalidKernel; zero block -> InvalidValue (both before
     # any device work, as in the reference wrappers VCRuntime.cpp:5584-5609).
     assert vc.vcLaunchKernel(None, 64, 32, []) == vc.VCError.InvalidKernel
-    err, k = vc.vcLoadKernel(None, "vadd")
+    err, k = vc.vcGetKernel("vadd")
     assert vc.vcLaunchKernel(k, 64, 0, []) == vc.VCError.InvalidValue
     vc.vcReleaseKernel(k)
     assert vc.vcMemcpy(None, None, 4, vc.VCMemcpyKind.HostToDevice) == vc.VCError.InvalidValue
@@ -115,7 +144,7 @@ def test_fault_injection_malloc_and_launch():
     out = _run_child(
         "from vkcuda_b200 import vc\n"
         "a = int(vc.vcMalloc(16)[0]); b = int(vc.vcMalloc(16)[0]); c = int(vc.vcMalloc(16)[0])\n"
-        "k = vc.vcLoadKernel(None, 'vadd')[1]\n"
+        "k = vc.vcGetKernel('vadd')[1]\n"
         "l1 = int(vc.vcLaunchKernel(k, 64, 32, [])); l2 = int(vc.vcLaunchKernel(k, 64, 32, []))\n"
         "print(a, b, c, l1, l2)\n",
         {"VC_FAULT_INJECT": "malloc:2,launch:1"})

@@ -33,7 +33,7 @@ def test_matmul_tiled_demo(gpu, dev, orc, N):
     A = (np.float32(0.1) * i + np.float32(0.01) * j).astype(np.float32)
     B = (np.float32(0.1) * j + np.float32(0.01) * i).astype(np.float32)
     dA, dB, dC = dev.put(A), dev.put(B), dev.alloc(N * N * 4)
-    err, k = gpu.vcLoadKernel(None, "matmulTiled")
+    err, k = gpu.vcGetKernel("matmulTiled")
     assert err == 0
     # The demo's launch: grid (N, N) elements, block 16 x 16.
     assert gpu.vcLaunchKernel2D(k, N, N, 16, 16, [gpu.ptr(dA.ptr), gpu.ptr(dB.ptr),
@@ -57,7 +57,7 @@ def test_vcfa_dump_of_our_kernel_passes_reference_criteria(gpu, dev, tmp_path, c
     nh, seq, hd = meta["nhead"], meta["seq"], meta["hdim"]
     Q, K, V, O_host = blobs["q"], blobs["k"], blobs["v"], blobs["o_hostref"]
     dq, dk, dv, do = dev.put(Q), dev.put(K), dev.put(V), dev.alloc(Q.nbytes)
-    err, k = gpu.vcLoadKernel(None, "flashAttn")
+    err, k = gpu.vcGetKernel("flashAttn")
     scale = np.float32(LOG2E / math.sqrt(hd))
     assert gpu.vcLaunchKernel(k, nh * seq, 16, [gpu.ptr(dq.ptr), gpu.ptr(dk.ptr), gpu.ptr(dv.ptr),
                                                 gpu.ptr(do.ptr), gpu.f32(scale),

@@ -36,7 +36,7 @@ def test_flash_attn_demo_legacy_launch(gpu, dev, causal):
     (nh, seq, hd, c), (Q, K, V, _, O_host) = load_vcfa(
         os.path.join(GOLDEN, f"fa_demo_causal{causal}.bin"))
     dq, dk, dv, do = dev.put(Q), dev.put(K), dev.put(V), dev.alloc(Q.nbytes)
-    err, k = gpu.vcLoadKernel(None, "flashAttn")
+    err, k = gpu.vcGetKernel("flashAttn")
     scale = np.float32(LOG2E / math.sqrt(hd))
     assert gpu.vcLaunchKernel(k, nh * seq, 16, [gpu.ptr(dq.ptr), gpu.ptr(dk.ptr), gpu.ptr(dv.ptr),
                                                 gpu.ptr(do.ptr), gpu.f32(scale),
@@ -52,7 +52,7 @@ def test_flash_attn_legacy_constants(gpu, dev, orc):
     Q, K, V = orc.fa_inputs(99, nh * seq * hd)
     scale = np.float32(LOG2E / math.sqrt(hd))
     dq, dk, dv, do = dev.put(Q), dev.put(K), dev.put(V), dev.alloc(Q.nbytes)
-    err, k = gpu.vcLoadKernel(None, "flashAttn")
+    err, k = gpu.vcGetKernel("flashAttn")
     for name, v in (("NHEAD", nh), ("SEQ", seq), ("HDIM", hd)):
         assert gpu.vcKernelSetConstant(k, name, v) == 0
     args = [gpu.ptr(dq.ptr), gpu.ptr(dk.ptr), gpu.ptr(dv.ptr), gpu.ptr(do.ptr), gpu.f32(scale),
@@ -170,6 +170,40 @@ def test_flash_tcgen05_config3_sampled(gpu, dev, orc):
     on a sample (4 slices x 64 rows, including the last rows of the sequence)."""
     _run_tc(gpu, dev, orc, 128, 4096, 128, True, False, seed=3, bh_check=(60, 64),
             row_check=(4032, 4096))
+
+
+def test_flash_tcgen05_config4_full_shape_sampled(gpu, orc):
+    """Benchmark config 4 at its own shape: bf16, B=32, H=32 (1024 slices),
+    N=8192, d=128, non-causal, Q/K/V ~ 0.5 N(0,1) rounded to bf16 (2 GiB per
+    tensor, generated on the device). The whole launch runs; the fp64 oracle
+    checks 4 slices (the first, the last, and both sides of an 8-GPU shard
+    boundary) x the first and last 64 query rows, within the bf16 bar."""
+    import torch
+    BH, N, d = 1024, 8192, 128
+    g = torch.Generator(device="cuda").manual_seed(4)
+
+    def gen():
+        return (torch.randn(BH, N, d, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+
+    q, k, v = gen(), gen(), gen()
+    o = torch.empty_like(q)
+    s = np.float32(LOG2E / math.sqrt(d))
+    torch.cuda.synchronize()
+    assert gpu.flash_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), BH, N, d, s,
+                         False, gpu.Dtype.BF16) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    assert gpu.kernel_error(True) == 0
+    slices = [0, 127, 128, 1023]
+    idx = torch.tensor(slices, device="cuda")
+    qs, ks, vs, os_ = (t.index_select(0, idx).float().cpu().numpy() for t in (q, k, v, o))
+    del q, k, v, o
+    torch.cuda.empty_cache()
+    assert np.isfinite(os_).all()
+    for rows in ((0, 64), (N - 64, N)):
+        ref = orc.attention(qs, ks, vs, len(slices), N, d, s, False,
+                            row_range=rows).reshape(len(slices), N, d)
+        err = np.abs(os_[:, rows[0]:rows[1]] - ref[:, rows[0]:rows[1]]).max()
+        assert err <= TOL["bf16"], (rows, err)
 
 
 def test_flash_rejects_bad_shapes(gpu, dev):

@@ -28,7 +28,7 @@ def test_wmma_gemm_demo_exact(gpu, dev, kat):
     B = np.array(kat["wmma_gemm"]["B"], np.float16)
     C = np.ones((8, 8), np.float32)
     dA, dB, dC, dD = dev.put(A), dev.put(B), dev.put(C), dev.alloc(256)
-    err, k = gpu.vcLoadKernel(None, "wmma_gemm")
+    err, k = gpu.vcGetKernel("wmma_gemm")
     assert gpu.vcLaunchKernel(k, 1, 32, [gpu.ptr(dA.ptr), gpu.ptr(dB.ptr), gpu.ptr(dC.ptr),
                                          gpu.ptr(dD.ptr)]) == 0
     assert gpu.vcDeviceSynchronize() == 0
@@ -47,7 +47,7 @@ def test_matmul_coopmat_demo_exact(gpu, dev, kat, N):
     A = ((n * 3 + m * 5) % 7).astype(np.float16)
     B = ((n * 2 + m * 3) % 7).astype(np.float16)
     dA, dB, dC = dev.put(A), dev.put(B), dev.alloc(N * L * 4)
-    err, k = gpu.vcLoadKernel(None, "matmulCoopmat")
+    err, k = gpu.vcGetKernel("matmulCoopmat")
     assert gpu.vcLaunchKernel2D(k, (N // 16) * 32, N // 16, 32, 1,
                                 [gpu.ptr(dA.ptr), gpu.ptr(dB.ptr), gpu.ptr(dC.ptr), gpu.i32(N)]) == 0
     assert gpu.vcDeviceSynchronize() == 0

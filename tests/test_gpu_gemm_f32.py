@@ -57,7 +57,7 @@ def test_matmul_tiled_demo_sizes_relative_1e4(gpu, dev, orc, N):
     sizes; N % 4 == 0 runs on the tensor cores."""
     A, B = _demo_inputs(N)
     dA, dB, dC = dev.put(A), dev.put(B), dev.alloc(N * N * 4)
-    err, k = gpu.vcLoadKernel(None, "matmulTiled")
+    err, k = gpu.vcGetKernel("matmulTiled")
     assert err == 0
     assert gpu.vcLaunchKernel2D(k, N, N, 16, 16, [gpu.ptr(dA.ptr), gpu.ptr(dB.ptr),
                                                   gpu.ptr(dC.ptr), gpu.i32(N)]) == 0
@@ -103,6 +103,13 @@ def test_gemm_f32_split_k_small_grid_deterministic(gpu, dev, orc, b_kn):
     ref = orc.gemm(A, B, M, N, K, K, ldb, b_kn, Cin=cin, ldc=N)
     mag = orc.gemm(np.abs(A), np.abs(B), M, N, K, K, ldb, b_kn)
     assert (np.abs(outs[0].astype(np.float64) - ref) <= BOUND * mag + 1e-6).all()
+    # In place (D is Cin): the same shape must not zero D before reading the
+    # addend, so it runs unsplit; same bar.
+    assert gpu.gemm(dA.ptr, dB.ptr, dC.ptr, dC.ptr, M, N, K, K, ldb, N, N,
+                    gpu.Dtype.F32, b_kn) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    inplace = dC.to_host(np.float32, M * N).reshape(M, N).astype(np.float64)
+    assert (np.abs(inplace - ref) <= BOUND * mag + 1e-6).all()
 
 
 def test_gemm_f32_with_addend_and_strides(gpu, dev, orc):
@@ -118,7 +125,7 @@ def test_gemm_f32_unaligned_strides_use_simt_path(gpu, dev, orc):
     N = 131
     A, B = _demo_inputs(N)
     dA, dB, dC = dev.put(A), dev.put(B), dev.alloc(N * N * 4)
-    err, k = gpu.vcLoadKernel(None, "matmulTiled")
+    err, k = gpu.vcGetKernel("matmulTiled")
     assert gpu.vcLaunchKernel2D(k, N, N, 16, 16, [gpu.ptr(dA.ptr), gpu.ptr(dB.ptr),
                                                   gpu.ptr(dC.ptr), gpu.i32(N)]) == 0
     assert gpu.vcDeviceSynchronize() == 0

@@ -100,7 +100,7 @@ def test_graph_record_replay(gpu, dev, orc):
     a = rng.random(n, dtype=np.float32)
     b = rng.random(n, dtype=np.float32)
     da, db, dc = dev.put(a), dev.put(b), dev.alloc(4 * n)
-    err, k = gpu.vcLoadKernel(None, "vadd")
+    err, k = gpu.vcGetKernel("vadd")
     err, g = gpu.vcGraphCreate()
     assert gpu.vcGraphBeginRecord(g) == 0
     assert gpu.vcLaunchKernel(k, n, 256, [gpu.ptr(da.ptr), gpu.ptr(db.ptr), gpu.ptr(dc.ptr),
@@ -169,7 +169,7 @@ def test_indirect_launch_reads_workgroups_from_device(gpu, dev, orc):
     # (1024 elements) are not launched and keep their zeros.
     ind = dev.put(np.array([7, 7, n // 256 - 4, 1, 1], np.uint32))
     assert gpu.vcMemset(dc.ptr, 0, 4 * n) == 0
-    err, k = gpu.vcLoadKernel(None, "vadd")
+    err, k = gpu.vcGetKernel("vadd")
     args = [gpu.ptr(da.ptr), gpu.ptr(db.ptr), gpu.ptr(dc.ptr), gpu.i32(n)]
     assert gpu.vcLaunchKernelIndirect(k, ind.ptr, 8, (256, 1, 1), args) == 0
     assert gpu.vcDeviceSynchronize() == 0
@@ -198,7 +198,7 @@ def test_profile_table_at_shutdown(gpu):
                "e, d = vc.vcMalloc(1 << 20)\n"
                "x = np.ones(1 << 18, np.float32)\n"
                "assert vc.vcMemcpy(d, x, x.nbytes, vc.VCMemcpyKind.HostToDevice) == 0\n"
-               "e, k = vc.vcLoadKernel(None, 'vadd')\n"
+               "e, k = vc.vcGetKernel('vadd')\n"
                "assert vc.vcLaunchKernel(k, 1 << 18, 256, [vc.ptr(d), vc.ptr(d), vc.ptr(d), vc.i32(1 << 18)]) == 0\n"
                "assert vc.vcDeviceSynchronize() == 0\n"
                "assert vc.vcShutdown() == 0\n", {"VC_PROFILE": "1"})

@@ -96,7 +96,7 @@ def test_legacy_vadd_and_reduce_demos(gpu, dev):
     a = np.array(kat["vadd"]["a"], np.float32)
     b = np.array(kat["vadd"]["b"], np.float32)
     da, db, dc = dev.put(a), dev.put(b), dev.alloc(64 * 4)
-    err, k = gpu.vcLoadKernel(None, "vadd")
+    err, k = gpu.vcGetKernel("vadd")
     assert err == 0
     assert gpu.vcLaunchKernel(k, 64, 32, [gpu.ptr(da.ptr), gpu.ptr(db.ptr), gpu.ptr(dc.ptr),
                                           gpu.i32(64)]) == 0
@@ -106,7 +106,7 @@ def test_legacy_vadd_and_reduce_demos(gpu, dev):
 
     x = np.arange(128, dtype=np.float32)
     dx, dout = dev.put(x), dev.alloc(4 * 4)
-    err, k = gpu.vcLoadKernel(None, "blockReduce")
+    err, k = gpu.vcGetKernel("blockReduce")
     assert gpu.vcLaunchKernel(k, 128, 32, [gpu.ptr(dx.ptr), gpu.ptr(dout.ptr), gpu.i32(128)]) == 0
     assert gpu.vcDeviceSynchronize() == 0
     assert dout.to_host(np.float32, 4).tolist() == kat["reduce"]["partials"]

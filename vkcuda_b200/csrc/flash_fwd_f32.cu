@@ -307,14 +307,7 @@ cudaError_t launch_dr(const FlashArgs &f, cudaStream_t stream) {
 // else 8 rows of 16 lanes.
 template <int D>
 cudaError_t launch_d(const FlashArgs &f, cudaStream_t stream) {
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        sms <= 0)
-      sms = 148;
-  }
+  const int sms = sm_count_current();
   const long long blocks8 = (long long)f.BH * ((f.N + 7) / 8);
   if (blocks8 >= 2LL * sms) return launch_dr<D, 8, 16, 2>(f, stream);
   // Grids too small to fill the GPU with 4-row blocks: up to d = 64, two

@@ -554,8 +554,21 @@ cudaError_t launch_gemm_f32_tcgen05(const GemmArgs &g, cudaStream_t stream) {
   // each half is at most one K chunk: both halves add onto a zeroed C, so
   // every element gets exactly two round-to-nearest adds onto zero and the
   // result does not depend on their order.
-  const int split_k =
-      (2 * pair_tiles <= resident && kblocks >= 2 && kblocks <= 2 * kChunkBlocks) ? 2 : 1;
+  // The split zeroes D before the kernel reads Cin, so it is taken only when
+  // Cin does not share memory with D (an in-place D == Cin keeps split_k = 1,
+  // where each element of Cin is read before the same element of D is stored).
+  bool cin_overlaps_d = false;
+  if (g.Cin) {
+    const uintptr_t d0 = reinterpret_cast<uintptr_t>(g.D);
+    const uintptr_t d1 = d0 + ((size_t)(g.M - 1) * (size_t)g.ldd + (size_t)g.N) * sizeof(float);
+    const uintptr_t c0 = reinterpret_cast<uintptr_t>(g.Cin);
+    const uintptr_t c1 = c0 + ((size_t)(g.M - 1) * (size_t)g.ldc + (size_t)g.N) * sizeof(float);
+    cin_overlaps_d = c0 < d1 && d0 < c1;
+  }
+  const int split_k = (!cin_overlaps_d && 2 * pair_tiles <= resident && kblocks >= 2 &&
+                       kblocks <= 2 * kChunkBlocks)
+                          ? 2
+                          : 1;
   int clusters, num_full, num_units;
   if (split_k == 2) {
     num_full = num_units = 2 * pair_tiles;

@@ -10,6 +10,8 @@
 namespace vcb {
 
 // ---- streaming (stream_kernels.cu)
+// SM count of the current device (cached per device).
+int sm_count_current();
 int stream_max_blocks();
 cudaError_t launch_vadd_f32(const float *a, const float *b, float *c, int64_t n,
                             cudaStream_t stream);
@@ -39,6 +41,16 @@ cudaError_t launch_sum_f32(const float *x, const float *b, float *c, int64_t n,
                            double *out, double *partials, unsigned int *ticket,
                            int max_blocks, cudaStream_t stream,
                            const PeerExchange *px = nullptr);
+// The sum of launch_sum_f32 (same grid, same order, bit-identical result)
+// with its block partials and ticket in a static device array of the library
+// instead of caller- or runtime-allocated memory. Allocates nothing. At most
+// noalloc_sum_capacity() blocks: a grid that needs more is refused with
+// cudaErrorInvalidValue and *blocks_needed says how many it needed.
+int noalloc_sum_capacity();
+cudaError_t launch_sum_f32_noalloc(const float *x, int64_t n, double *out, cudaStream_t stream,
+                                   int *blocks_needed);
+// a[i] = base + i for i < n (the multi-device demo's pattern fill).
+cudaError_t launch_fill_pattern(int *a, int base, int64_t n, cudaStream_t stream);
 cudaError_t launch_block_reduce_demo(const float *in, float *out, int n, int block,
                                      int groups, cudaStream_t stream);
 

@@ -1094,6 +1094,21 @@ VCError k_vadd(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, int n, c
   return run(vcb::launch_vadd_f32((const float *)pa, (const float *)pb, (float *)pc, m, s), "vadd");
 }
 
+// fillPattern(int *a, int base, int n): a[i] = base + i for
+// i < min(n, workgroups*block) (test/multigpu.vc:24-27).
+VCError k_fill_pattern(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, int n,
+                       cudaStream_t s) {
+  const void *pa;
+  long long base, cnt;
+  if (!arg_ptr(a, n, 0, &pa) || !arg_i64(a, n, 1, &base) || !arg_i64(a, n, 2, &cnt) || n != 3)
+    return bad_args("fillPattern");
+  long long covered = (long long)sh.wgx * sh.bx * sh.wgy * sh.by;
+  long long m = cnt < covered ? cnt : covered;
+  if (m <= 0) return VCError::Success;
+  if ((size_t)m * 4 > bytes_available(pa)) return too_small("fillPattern");
+  return run(vcb::launch_fill_pattern((int *)pa, (int)base, m, s), "fillPattern");
+}
+
 // blockReduce(in, out, int N): out[g] = tree sum of block g (test/reduce.vc).
 VCError k_block_reduce(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, int n,
                        cudaStream_t s) {
@@ -1339,6 +1354,7 @@ const std::vector<KernelEntry> &registry() {
   static const std::vector<KernelEntry> r = {
       {"vadd", k_vadd, {}},
       {"blockReduce", k_block_reduce, {}},
+      {"fillPattern", k_fill_pattern, {}},
       {"flashAttn", k_flash_attn, {{"NHEAD", 2}, {"SEQ", 64}, {"HDIM", 16}, {"BR", 16}, {"BC", 16}}},
       {"wmma_gemm", k_wmma_gemm, {}},
       {"matmulCoopmat", k_matmul_coopmat, {{"L", 1024}}},
@@ -1392,12 +1408,18 @@ VCError vcGetKernel(const char *name, VCKernelHandle *outKernel) {
   return VCError::Success;
 }
 
+// The reference refuses, with InvalidValue, any module that is missing, shorter
+// than the 5-word SPIR-V header or without the SPIR-V magic number, before it
+// looks at the entry point (lib/Runtime/VCRuntime.cpp:4261-4268). Callers that
+// hold no module resolve a kernel by name with vcGetKernel instead.
 VCError vcLoadKernel(const uint32_t *spirvWords, size_t wordCount, const char *entryPoint,
                      VCKernelHandle *outKernel) {
   if (!outKernel) return VCError::InvalidValue;
-  if (spirvWords && wordCount > 0 && spirvWords[0] != 0x07230203u) {
-    std::fprintf(stderr, "vc: module is not SPIR-V (bad magic)\n");
-    return VCError::InvalidKernel;
+  if (!spirvWords || wordCount < 5 || spirvWords[0] != 0x07230203u) {
+    std::fprintf(stderr,
+                 "vc: kernel '%s': input is not a SPIR-V binary (no 0x07230203 magic word)\n",
+                 entryPoint ? entryPoint : "?");
+    return VCError::InvalidValue;
   }
   const char *name = entryPoint ? entryPoint : "main";
   const KernelEntry *e = find_entry(name);
@@ -1419,9 +1441,10 @@ VCError vcLoadKernelFromFile(const char *path, const char *entryPoint, VCKernelH
   std::ifstream f(path, std::ios::binary);
   if (!f) return VCError::InvalidValue;
   std::vector<char> bytes((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
-  if (bytes.size() < 4 || bytes.size() % 4) return VCError::InvalidKernel;
-  std::vector<uint32_t> words(bytes.size() / 4);
-  std::memcpy(words.data(), bytes.data(), bytes.size());
+  // Whole words, the last one zero-padded, as the reference reads a file
+  // (VCRuntime.cpp:4378-4387); vcLoadKernel then judges the module.
+  std::vector<uint32_t> words((bytes.size() + 3) / 4, 0u);
+  if (!bytes.empty()) std::memcpy(words.data(), bytes.data(), bytes.size());
   return vcLoadKernel(words.data(), words.size(), entryPoint, outKernel);
 }
 
@@ -1646,6 +1669,9 @@ int vc_graph_reset(void *g) { return E(vcGraphReset(static_cast<VCGraphHandle>(g
 int vc_load_kernel(const uint32_t *words, size_t n, const char *entry, void **out) {
   return E(vcLoadKernel(words, n, entry, reinterpret_cast<VCKernelHandle *>(out)));
 }
+int vc_load_kernel_from_file(const char *path, const char *entry, void **out) {
+  return E(vcLoadKernelFromFile(path, entry, reinterpret_cast<VCKernelHandle *>(out)));
+}
 int vc_release_kernel(void *k) { return E(vcReleaseKernel(static_cast<VCKernelHandle>(k))); }
 int vc_launch_kernel(void *k, unsigned grid, unsigned block, const vc_kernel_arg *args, int n) {
   static_assert(sizeof(vc_kernel_arg) == sizeof(VCKernelArg), "layout");
@@ -1708,6 +1734,23 @@ int vc_sum_f32(const float *x, int64_t n, double *out, void *s) {
   if (!ensure_init()) return E(VCError::InitializationError);
   use_current_device();
   return E(sum_common(x, nullptr, nullptr, n, out, reinterpret_cast<cudaStream_t>(s), "vc_sum_f32"));
+}
+// No reference counterpart: vc_sum_f32 for callers that cannot allocate (see
+// include/vc_b200.h). Same prologue and error mapping as vc_sum_f32; the
+// scratch is the static device array of stream_kernels.cu.
+int vc_sum_f32_noalloc(const float *x, int64_t n, double *out, void *s) {
+  if (!x || !out || n < 0) return E(VCError::InvalidValue);
+  if (!ensure_init()) return E(VCError::InitializationError);
+  use_current_device();
+  int needed = 0;
+  cudaError_t e = vcb::launch_sum_f32_noalloc(x, n, out, reinterpret_cast<cudaStream_t>(s), &needed);
+  if (e == cudaErrorInvalidValue && needed > vcb::noalloc_sum_capacity()) {
+    std::fprintf(stderr,
+                 "vc_sum_f32_noalloc: this device needs %d block partials; the static scratch "
+                 "holds %d\n", needed, vcb::noalloc_sum_capacity());
+    return E(VCError::InvalidValue);
+  }
+  return E(map_cuda(e, "vc_sum_f32_noalloc"));
 }
 int vc_vadd_sum_f32(const float *a, const float *b, float *c, int64_t n, double *out, void *s) {
   if (!a || !b || !c || !out || n < 0) return E(VCError::InvalidValue);

@@ -258,14 +258,17 @@ __global__ void block_reduce_demo_kernel(const float *__restrict__ in,
 
 __global__ void fill_f64_kernel(double *p, double v) { *p = v; }
 
+// a[i] = base + i for i < n (test/multigpu.vc:24-27, the multi-device demo's
+// pattern fill), grid-stride.
+__global__ void fill_pattern_kernel(int *__restrict__ a, int base, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride)
+    a[i] = base + static_cast<int>(i);
+}
+
 int stream_grid(int64_t work_items) {
-  static int sm_count = 0;
-  if (sm_count == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-    if (sm_count <= 0) sm_count = 148;
-  }
+  const int sm_count = sm_count_current();
   // Four resident 512-thread CTAs per SM (2048 threads) keep ~128 KiB in
   // flight per SM; fewer CTAs when the array is small.
   const int64_t full = static_cast<int64_t>(sm_count) * 4;
@@ -278,12 +281,26 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-int stream_max_blocks() {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms * 4;
+int sm_count_current() {
+  // One slot per device (the grid of every streaming launch depends on the
+  // SM count of the device it runs on); filled on first use, racing threads
+  // store the same value.
+  constexpr int kMaxDevices = 64;
+  static int by_device[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int *slot = (dev >= 0 && dev < kMaxDevices) ? &by_device[dev] : nullptr;
+  int sms = slot ? __atomic_load_n(slot, __ATOMIC_RELAXED) : 0;
+  if (sms <= 0) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms <= 0)
+      return 148;
+    if (slot) __atomic_store_n(slot, sms, __ATOMIC_RELAXED);
+  }
+  return sms;
 }
+
+int stream_max_blocks() { return sm_count_current() * 4; }
 
 cudaError_t launch_vadd_f32(const float *a, const float *b, float *c, int64_t n,
                             cudaStream_t stream) {
@@ -340,6 +357,12 @@ cudaError_t launch_sum_f32(const float *x, const float *b, float *c, int64_t n,
       sum_scalar_kernel<false><<<grid, kStreamThreads, 0, stream>>>(
           x, nullptr, nullptr, n, partials, ticket, out, px);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill_pattern(int *a, int base, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  fill_pattern_kernel<<<stream_grid(n / kUnroll + 1), kStreamThreads, 0, stream>>>(a, base, n);
   return cudaGetLastError();
 }
 
@@ -405,41 +428,25 @@ static cudaError_t noalloc_scratch_address(NoAllocSumScratch **out) {
   return cudaSuccess;
 }
 
-}  // namespace vcb
+int noalloc_sum_capacity() { return kNoAllocMaxPartials; }
 
-VCB_DEFINE_ERROR_ACCESSOR(stream_kernels_error)
-
-// *out = sum of x[0..n) (device double), like vc_sum_f32, without allocating
-// anything: scratch lives in the library's static device array (see above).
-// The first call on a device looks up that array's address (no allocation);
-// make that first call before any stream capture. Runs on the calling
-// thread's current CUDA device.
-extern "C" int vc_sum_f32_noalloc(const float *x, int64_t n, double *out, void *stream) {
-  using namespace vcb;
-  if (!x || !out || n < 0) return VC_INVALID_VALUE;
+cudaError_t launch_sum_f32_noalloc(const float *x, int64_t n, double *out, cudaStream_t stream,
+                                   int *blocks_needed) {
+  if (n < 0) return cudaErrorInvalidValue;
   const bool vec = aligned16(x);
   const int64_t units = vec ? (n / 4) / kUnroll + 1 : n / kUnroll + 1;
   const int grid = stream_grid(units);
-  if (grid > kNoAllocMaxPartials) {
-    std::fprintf(stderr,
-                 "vc_sum_f32_noalloc: this device needs %d block partials; the static scratch "
-                 "holds %d\n", grid, kNoAllocMaxPartials);
-    return VC_INVALID_VALUE;
-  }
+  if (blocks_needed) *blocks_needed = grid;
+  if (grid > kNoAllocMaxPartials) return cudaErrorInvalidValue;
   NoAllocSumScratch *scratch = nullptr;
   cudaError_t e = noalloc_scratch_address(&scratch);
-  if (e != cudaSuccess) {
-    std::fprintf(stderr, "vc_sum_f32_noalloc: scratch lookup failed: %s\n", cudaGetErrorString(e));
-    return VC_UNKNOWN;
-  }
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  e = cudaMemsetAsync(&scratch->ticket, 0, sizeof(unsigned int), s);
-  if (e == cudaSuccess)
-    e = launch_sum_f32(x, nullptr, nullptr, n, out, scratch->partials, &scratch->ticket,
-                       kNoAllocMaxPartials, s);
-  if (e != cudaSuccess) {
-    std::fprintf(stderr, "vc_sum_f32_noalloc: %s\n", cudaGetErrorString(e));
-    return VC_UNKNOWN;
-  }
-  return VC_SUCCESS;
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(&scratch->ticket, 0, sizeof(unsigned int), stream);
+  if (e != cudaSuccess) return e;
+  return launch_sum_f32(x, nullptr, nullptr, n, out, scratch->partials, &scratch->ticket,
+                        kNoAllocMaxPartials, stream);
 }
+
+}  // namespace vcb
+
+VCB_DEFINE_ERROR_ACCESSOR(stream_kernels_error)

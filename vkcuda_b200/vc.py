@@ -12,7 +12,7 @@ arrays, ``bytes``/``bytearray``, ctypes objects or integer addresses.
     vc.vcInit()
     err, d_a = vc.vcMalloc(n * 4)
     vc.vcMemcpy(d_a, host_a, n * 4, vc.VCMemcpyKind.HostToDevice)
-    err, k = vc.vcLoadKernel(None, "vadd")
+    err, k = vc.vcGetKernel("vadd")
     vc.vcLaunchKernel(k, n, 256, [vc.ptr(d_a), vc.ptr(d_b), vc.ptr(d_c), vc.i32(n)])
 """
 from __future__ import annotations
@@ -127,6 +127,7 @@ SIGNATURES = {
     "vc_graph_begin_record": (_I, [_VP]), "vc_graph_end_record": (_I, [_VP]),
     "vc_graph_launch": (_I, [_VP, _VP]), "vc_graph_reset": (_I, [_VP]),
     "vc_load_kernel": (_I, [ctypes.POINTER(ctypes.c_uint32), _SZ, ctypes.c_char_p, _PVP]),
+    "vc_load_kernel_from_file": (_I, [ctypes.c_char_p, ctypes.c_char_p, _PVP]),
     "vc_release_kernel": (_I, [_VP]),
     "vc_launch_kernel": (_I, [_VP, _U, _U, ctypes.POINTER(VCKernelArg), _I]),
     "vc_launch_kernel_s": (_I, [_VP, _U, _U, ctypes.POINTER(VCKernelArg), _I, _VP]),
@@ -384,9 +385,11 @@ def vcGraphReset(g) -> VCError: return VCError(library().vc_graph_reset(g))
 
 
 def vcLoadKernel(words, entry: str) -> Tuple[VCError, int]:
-    """`words`: a sequence of uint32 SPIR-V words, or None to resolve by name only."""
+    """`words`: a sequence of uint32 SPIR-V words; a missing module, one shorter
+    than the 5-word header or without the SPIR-V magic is InvalidValue, as in
+    the reference. vcGetKernel resolves a kernel by name without a module."""
     k = ctypes.c_void_p(0)
-    if words is None:
+    if not words:
         e = library().vc_load_kernel(None, 0, entry.encode(), ctypes.byref(k))
     else:
         arr = (ctypes.c_uint32 * len(words))(*words)
@@ -455,15 +458,11 @@ vcLaunchKernelIndirectS = vcLaunchKernelIndirect
 
 
 def vcLoadKernelFromFile(path: str, entry: str) -> Tuple[VCError, int]:
-    """Load a module from a file (whole 32-bit words) and resolve `entry`."""
-    try:
-        data = open(path, "rb").read()
-    except OSError:
-        return VCError.InvalidValue, 0
-    if len(data) < 4 or len(data) % 4:
-        return VCError.InvalidKernel, 0
-    import struct
-    return vcLoadKernel(list(struct.unpack(f"<{len(data) // 4}I", data)), entry)
+    """Load a module from a file and resolve `entry` (the library reads the
+    file: whole 32-bit words, the last zero-padded)."""
+    k = ctypes.c_void_p(0)
+    e = library().vc_load_kernel_from_file(path.encode(), entry.encode(), ctypes.byref(k))
+    return VCError(e), (k.value or 0)
 
 
 def vcErrorString(err) -> str:
