@@ -200,6 +200,9 @@ def check(err, what):
 
 
 IDLE_BEFORE_S = 1.0  # every workload starts from an idle GPU (as the peaks were measured)
+# A timed region of at least this many ms of back-to-back launches is judged
+# against the sustained (power-capped) peak, a shorter one against burst.
+SUSTAINED_REGION_MS = 1000.0
 
 
 def timed(dist, stream, fn, steps, warmup, sampler=None, stats=None):
@@ -240,14 +243,38 @@ class _Null:
 
 
 # ---------------------------------------------------------------- workloads
+def colsum_parity(dist, A, B, C):
+    """Cross-rank check of a product split over the ranks by M-blocks (rank r
+    holds rows of A and C, B replicated): the column sums of the assembled C
+    (summed over the ranks) against (column sums of the assembled A) * B, in
+    fp64. Returns the largest |difference| over the columns in units of the
+    bar sqrt(M_total) * 1e-3 * sqrt(K) (each element within 1e-3 sqrt(K),
+    errors of independent rows adding as a random walk); <= 1 passes."""
+    import torch
+    K = A.shape[1]
+    cs = C.double().sum(0)
+    asum = A.double().sum(0)
+    rows = torch.tensor([float(A.shape[0])], dtype=torch.float64, device="cuda")
+    if dist.pg:
+        for t in (cs, asum, rows):
+            dist.pg.all_reduce(t)
+    ref = asum @ B.double()
+    bar = math.sqrt(rows.item()) * 1e-3 * math.sqrt(K)
+    return float((cs - ref).abs().max().item() / bar)
+
+
 def gemm_workload(vc, dist, steps, warmup, pk, device_uuid, want_e2e=True):
+    """Rank r computes rows [4096 r, 4096 (r + 1)) of one (4096 N_ranks) x
+    4096 x 4096 product: its own M-block of A, B the same on every rank
+    (generated from one seed), no communication."""
     import torch
     N = GEMM_N
-    g = torch.Generator(device="cuda").manual_seed(1 + dist.rank)
+    ga = torch.Generator(device="cuda").manual_seed(1 + dist.rank)
+    gb = torch.Generator(device="cuda").manual_seed(1000)
     sets = []
     for _ in range(ROTATE):
-        A = (torch.rand(N, N, device="cuda", generator=g) * 2 - 1).half()
-        B = (torch.rand(N, N, device="cuda", generator=g) * 2 - 1).half()
+        A = (torch.rand(N, N, device="cuda", generator=ga) * 2 - 1).half()
+        B = (torch.rand(N, N, device="cuda", generator=gb) * 2 - 1).half()
         C = torch.empty(N, N, device="cuda", dtype=torch.float32)
         sets.append((A, B, C))
     stream = torch.cuda.current_stream()
@@ -268,9 +295,12 @@ def gemm_workload(vc, dist, steps, warmup, pk, device_uuid, want_e2e=True):
     torch.cuda.synchronize()
     A, B, C = sets[0]
     ref = A[:64].float() @ B.float()
-    err = (C[:64] - ref).abs().max().item()
+    err = dist.max((C[:64] - ref).abs().max().item())
     if not err <= 1e-3 * math.sqrt(N):
         raise RuntimeError(f"GEMM parity guard failed: max err {err}")
+    colsum = dist.max(colsum_parity(dist, A, B, C))
+    if not colsum <= 1.0:
+        raise RuntimeError(f"GEMM cross-rank column-sum check failed: {colsum}")
 
     sampler = ClockSampler(device_uuid)
     step_stats = {}
@@ -279,9 +309,10 @@ def gemm_workload(vc, dist, steps, warmup, pk, device_uuid, want_e2e=True):
     per_launch_ms = ms / (steps * GEMMS_PER_STEP)
     value = flop_step * steps * dist.world / (ms * 1e-3) / 1e12
     achieved = 2.0 * N ** 3 / (per_launch_ms * 1e-3) / 1e12
-    # The timed region runs the kernel back to back; longer than ~0.2 s it is
-    # the power-capped regime the sustained peak was measured in.
-    sustained = ms > 200.0
+    # The timed region runs the kernel back to back; a region of a second or
+    # more is the power-capped regime the sustained peak was measured in
+    # (seconds of back-to-back GEMMs); a shorter one is judged against burst.
+    sustained = ms >= SUSTAINED_REGION_MS
     peak = pk["bf16_sustained"] if sustained else pk["bf16"]
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s",
@@ -296,6 +327,8 @@ def gemm_workload(vc, dist, steps, warmup, pk, device_uuid, want_e2e=True):
                      "traffic": traffic_table().get("gemm_f16_4096")},
         "clocks": sampler.summary(),
         "gpu_launches": steps * GEMMS_PER_STEP,
+        "parity": {"row_sample_max_err_all_ranks": err, "bar": 1e-3 * math.sqrt(N),
+                   "colsum_all_ranks_over_bar": round(colsum, 5), "ranks": dist.world},
     }
     if want_e2e:
         # 32 steps (~50 ms): the first upload and the last download, which
@@ -411,6 +444,78 @@ def gemm_e2e(vc, dist, steps, warmup):
                     "directions busy (64 MiB each way per step)"}
 
 
+MBLOCK_M = 8 * GEMM_N  # rows of the one product the M-block GEMM splits over the ranks
+MBLOCK_PER_STEP = 20
+
+
+def gemm_mblock_workload(vc, dist, steps, warmup, pk):
+    """One product C = A * B of MBLOCK_M x 4096 x 4096 (fp16 in, fp32 out)
+    split over the ranks by M-blocks: rank r owns a contiguous share of the
+    rows of A and C, B (32 MiB) is the same on every rank, no communication
+    (strong scaling: the total work is fixed, at 8 ranks each computes a
+    4096^3 block). A step is MBLOCK_PER_STEP products, alternating over two
+    sets of A and C. Whole-job TFLOP/s = the product's FLOP / the slowest
+    rank's time; the assembled result is checked across the ranks by column
+    sums."""
+    import torch
+    N = GEMM_N
+    r0, r1 = shard(MBLOCK_M, dist.world, dist.rank)
+    m = r1 - r0
+    gb = torch.Generator(device="cuda").manual_seed(2000)
+    B = (torch.rand(N, N, device="cuda", generator=gb) * 2 - 1).half()
+    sets = []
+    for si in range(2):
+        ga = torch.Generator(device="cuda").manual_seed(3000 + 100 * si + dist.rank)
+        A = (torch.rand(m, N, device="cuda", generator=ga) * 2 - 1).half()
+        sets.append((A, torch.empty(m, N, device="cuda", dtype=torch.float32)))
+    stream = torch.cuda.current_stream()
+    state = {"i": 0}
+
+    def one():
+        A, C = sets[state["i"] % 2]
+        state["i"] += 1
+        check(vc.gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), None, m, N, N, N, N, N, 0,
+                      vc.Dtype.F16, True, stream.cuda_stream), "vc_gemm")
+
+    def step():
+        for _ in range(MBLOCK_PER_STEP):
+            one()
+
+    one()
+    torch.cuda.synchronize()
+    A, C = sets[0]
+    ref = A[-64:].float() @ B.float()
+    err = dist.max((C[-64:] - ref).abs().max().item())
+    colsum = dist.max(colsum_parity(dist, A, B, C))
+    if not (err <= 1e-3 * math.sqrt(N) and colsum <= 1.0):
+        raise RuntimeError(f"M-block GEMM parity failed: {err}, {colsum}")
+    step_stats = {}
+    ms = timed(dist, stream, step, steps, warmup, stats=step_stats)
+    per_launch = ms / (steps * MBLOCK_PER_STEP)
+    value = 2.0 * MBLOCK_M * N * N / (per_launch * 1e-3) / 1e12
+    achieved = 2.0 * m * N * N / (per_launch * 1e-3) / 1e12
+    sustained = ms >= SUSTAINED_REGION_MS
+    peak = pk["bf16_sustained"] if sustained else pk["bf16"]
+    res = {"workload": "gemm_mblock", "value": round(value, 2), "unit": "TFLOP/s",
+           "ms_per_step": round(ms / steps, 4), "per_launch_ms": round(per_launch, 5),
+           "ms_per_step_median": step_stats["median_ms"], "ms_per_step_best": step_stats["best_ms"],
+           "scaling": "strong",
+           "config": {"M": MBLOCK_M, "N": N, "K": N, "dtype": "f16 in, f32 out",
+                      "rows_per_rank": m, "gemms_per_step": MBLOCK_PER_STEP,
+                      "split": "M-blocks of one product, B replicated, no collective"},
+           "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                        "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                        "peak_kind": ("bf16 dense sustained" if sustained else "bf16 dense burst")
+                        + f" ({pk['source']}); timed region {ms / 1e3:.2f} s",
+                        "frac_vs_burst": round(achieved / pk["bf16"], 4), "traffic": None},
+           "gpu_launches": steps * MBLOCK_PER_STEP,
+           "parity": {"row_sample_max_err_all_ranks": err,
+                      "colsum_all_ranks_over_bar": round(colsum, 5), "ranks": dist.world}}
+    del sets, B
+    torch.cuda.empty_cache()
+    return res
+
+
 def gemm_f32_workload(vc, dist, steps, warmup, pk):
     """fp32 C = A * B at 4096^3 (the reference's fp32 GEMM, matmulTiled in
     examples/matmul_bench.vc, at the headline size): tensor-core path, hi*hi
@@ -454,7 +559,7 @@ def gemm_f32_workload(vc, dist, steps, warmup, pk):
     per_launch = ms / (steps * per_step)
     value = 2.0 * N ** 3 * dist.world / (per_launch * 1e-3) / 1e12
     achieved = 4.0 * N ** 3 / (per_launch * 1e-3) / 1e12
-    sustained = ms > 200.0
+    sustained = ms >= SUSTAINED_REGION_MS
     peak = round((pk["bf16_sustained"] if sustained else pk["bf16"]) / 2, 1)
     # CUDA-core path of the same call: A with a row stride of N + 1 floats.
     Ap = torch.zeros(N, N + 1, device="cuda")
@@ -535,7 +640,9 @@ def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk,
         q[:, -32:], K[-1:].float(), V[-1:].float(), is_causal=False,
         attn_mask=(torch.arange(N, device="cuda")[None, :] <= torch.arange(N - 32, N, device="cuda")[:, None])
         if causal else None)
-    perr = (O[-1:, -32:].float() - ref).abs().max().item()
+    # Every rank checks the last slice of its own shard; the line carries the
+    # largest error over the ranks.
+    perr = dist.max((O[-1:, -32:].float() - ref).abs().max().item())
     tol = {vc.Dtype.F16: 2e-3, vc.Dtype.BF16: 1e-2, vc.Dtype.F32: 1e-4}[dtype]
     if not perr <= tol:
         raise RuntimeError(f"{name} parity guard failed: {perr}")
@@ -546,7 +653,7 @@ def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk,
     value = flop / (per_launch * 1e-3) / 1e12 if shard_bh else flop * dist.world / (per_launch * 1e-3) / 1e12
     local_flop = (2.0 if causal else 4.0) * bh * N * N * d
     achieved = local_flop / (per_launch * 1e-3) / 1e12
-    long_kernel = per_launch > 10.0 or ms > 200.0
+    long_kernel = ms >= SUSTAINED_REGION_MS
     peak = pk["bf16_sustained"] if long_kernel else pk["bf16"]
     res = {"workload": name, "value": round(value, 2), "unit": "TFLOP/s",
            "ms_per_step": round(per_launch, 4), "ms_per_step_median": step_stats["median_ms"],
@@ -561,7 +668,10 @@ def flash_workload(vc, dist, name, B, H, N, d, causal, dtype, steps, warmup, pk,
                         + f" ({pk['source']}); timed region {ms / 1e3:.2f} s",
                         "frac_vs_burst": round(achieved / pk["bf16"], 4),
                         "traffic": flash_traffic(name, bh)},
-           "gpu_launches": steps * per_step, "parity_guard_max_err": perr}
+           "gpu_launches": steps * per_step, "parity_guard_max_err": perr,
+           "parity": {"check": "last 32 query rows of the last slice of every rank's shard vs "
+                               "torch fp32 SDPA", "max_err_all_ranks": perr, "bar": tol,
+                      "ranks": dist.world}}
     if dtype == vc.Dtype.F32:
         res["roofline"]["note"] = "fp32 CUDA-core path; latency bound at this size"
         res["launches_per_step"] = per_step
@@ -620,7 +730,8 @@ def stream_workload(vc, dist, steps, warmup, pk, log2n=30):
     ref = c.double().sum()
     if dist.pg:
         dist.pg.all_reduce(ref)
-    if not abs(total - ref.item()) <= 1e-6 * abs(ref.item()):
+    rel = dist.max(abs(total - ref.item()) / abs(ref.item()))
+    if not rel <= 1e-6:
         raise RuntimeError(f"stream parity guard failed: {total} vs {ref.item()}")
     ms_fused = timed(dist, stream, fused, steps, warmup)
     ms_vadd = timed(dist, stream, vadd_only, steps, warmup)
@@ -652,37 +763,226 @@ def stream_workload(vc, dist, steps, warmup, pk, log2n=30):
                                 "sum_frac": round(sum_gbs / pk["hbm"], 4)},
            "allreduce_us": round(ms_ar / steps * 1e3, 2) if ms_ar is not None else None,
            "nccl_step_ms": round(ms_nccl / steps, 4) if ms_nccl is not None else None,
-           "gpu_launches": steps, "sum_check_rel_err": abs(total - ref.item()) / abs(ref.item())}
+           "gpu_launches": steps, "sum_check_rel_err": rel,
+           "parity": {"check": "every rank's combined sum vs the fp64 sum of c all-reduced "
+                               "over the ranks", "max_rel_err_all_ranks": rel, "bar": 1e-6,
+                      "ranks": dist.world}}
     del a, b, c
     torch.cuda.empty_cache()
     return res
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_gemm_baseline(target_s=8.0):
-    """The oracle's fp64 GEMM (the demos' host reference loop) on a bounded
-    sample of C's rows, all host threads; TFLOP/s extrapolated per row."""
+# The reference's CPU path for each configuration is the demos' host loops,
+# restated in the oracle (oracle/oracle.c): fp64 GEMM rows
+# (matmul_coopmat_bench.vc:171-176), referenceAttn rows (flash_attn.vc:129-165),
+# vadd and the sum (test/vadd.vc:40-43, test/reduce.vc:64-75). Each is timed on
+# this box's host cores at 1 thread (the demos' form) and at all threads
+# (OpenMP over rows / elements), on a bounded sample of the configuration's
+# own work, and extrapolated by the work the sample covers (stated per entry).
+def cpu_info():
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    avail = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    return {"cpu_model": model, "nproc": os.cpu_count(), "threads_available": avail}
+
+
+def _cpu_threads():
+    # All host cores this process may run on (torchrun sets OMP_NUM_THREADS=1
+    # for its workers; the oracle takes the thread count explicitly).
+    return cpu_info()["threads_available"]
+
+
+def _timed_sample(run, units_min, units_max, target_s):
+    """run(units) -> None. Calibrates on units_min, then times calls on as
+    many units as target_s allows (at most units_max); a call shorter than
+    0.1 s is repeated and averaged. Returns (units, seconds per call)."""
+    t0 = time.perf_counter()
+    run(units_min)
+    dt = time.perf_counter() - t0
+    units = int(min(units_max, max(units_min, units_min * target_s / max(dt, 1e-4))))
+    est = dt * units / units_min
+    reps = 1 if est >= 0.1 else int(min(1000, math.ceil(0.1 / max(est, 1e-5))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        run(units)
+    return units, (time.perf_counter() - t0) / reps
+
+
+def _baseline(unit, kind_desc, measure, target_s):
+    """measure(threads, target_s) -> (value, sample text, seconds)."""
+    threads = _cpu_threads()
+    v_all, sample_all, s_all = measure(threads, target_s)
+    v_one, sample_one, s_one = measure(1, target_s / 2)
+    out = {"value": round(v_all, 6), "unit": unit, "cores": threads, "kind": "port",
+           "sample": f"{sample_all}, {s_all:.4g} s per call at {threads} threads; {kind_desc}",
+           "threads_1": round(v_one, 6), "threads_1_sample": f"{sample_one}, {s_one:.4g} s per call",
+           "seconds": round(s_all + s_one, 2)}
+    out.update(cpu_info())
+    return out
+
+
+def cpu_gemm_baseline(target_s=4.0, N=GEMM_N, fp32_inputs=False):
+    """fp64 GEMM loop over C's rows (A, B: fp16-rounded U[-1,1), or fp32 for
+    the fp32 config); TFLOP/s = 2 * rows * N^2 / seconds."""
+    from oracle import oracle
+    rng = np.random.default_rng(7)
+    a = rng.random((N, N), dtype=np.float32) * 2 - 1
+    b = rng.random((N, N), dtype=np.float32) * 2 - 1
+    if not fp32_inputs:
+        a = a.astype(np.float16).astype(np.float32)
+        b = b.astype(np.float16).astype(np.float32)
+
+    def measure(threads, budget):
+        rows, dt = _timed_sample(
+            lambda r: oracle.gemm(a, b, N, N, N, N, N, True, rows=(0, r), threads=threads),
+            max(2, threads), N, budget)
+        return 2.0 * rows * N * N / dt / 1e12, f"{rows} of {N} rows of C", dt
+
+    return _baseline("TFLOP/s", f"fp64 loop over {'fp32' if fp32_inputs else 'fp16'} inputs "
+                     f"(matmul_coopmat_bench.vc:171-176 form), {N}^3, extrapolated per row",
+                     measure, target_s)
+
+
+def cpu_attention_baseline(BH, N, d, causal, target_s=4.0):
+    """referenceAttn (fp64, two passes per row) over a sample of query rows of
+    one slice, taken from the end of the slice (the heaviest rows when
+    causal), extrapolated to all BH * N rows by the keys each row visits
+    (N per row; i + 1 for causal row i). FLOP counted as the configuration
+    counts them (4 BH N^2 d; half of it causal)."""
+    from oracle import oracle
+    rng = np.random.default_rng(9)
+    q, k, v = (rng.standard_normal(N * d).astype(np.float32) for _ in range(3))
+    out = np.zeros(N * d, np.float32)
+    scale = LOG2E / math.sqrt(d)
+    job_flop = (2.0 if causal else 4.0) * BH * N * N * d
+    keys_all = BH * (N * (N + 1) / 2 if causal else float(N) * N)
+
+    def keys(r0, r1):
+        return (r1 * (r1 + 1) - r0 * (r0 + 1)) / 2 if causal else float(r1 - r0) * N
+
+    def measure(threads, budget):
+        rows, dt = _timed_sample(
+            lambda r: oracle.attention(q, k, v, 1, N, d, scale, causal, row_range=(N - r, N),
+                                       threads=threads, out=out),
+            min(N, max(4, threads)), N, budget)
+        t_full = dt * keys_all / keys(N - rows, N)
+        return job_flop / t_full / 1e12, f"the last {rows} of {N} rows of 1 of {BH} slices", dt
+
+    return _baseline("TFLOP/s", f"referenceAttn fp64 rows (flash_attn.vc:129-165), "
+                     f"BH={BH} N={N} d={d} causal={int(causal)}, extrapolated by keys visited",
+                     measure, target_s)
+
+
+def cpu_stream_baseline(log2n=30, reps=2):
+    """vadd (c = a + b, fp32) then the fp64 sum of c over the whole 2^log2n
+    arrays; GB/s at 12 bytes per element (the fused pair's accounting)."""
+    from oracle import oracle
+    n = 1 << log2n
+    a = np.full(n, 0.25, np.float32)
+    b = np.full(n, 0.5, np.float32)
+    c = np.empty_like(a)
+    L = oracle.lib()
+    L.oracle_vadd(a.ctypes.data, b.ctypes.data, c.ctypes.data, n, 0)  # first touch, untimed
+
+    def measure(threads, _budget):
+        best = None
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            L.oracle_vadd(a.ctypes.data, b.ctypes.data, c.ctypes.data, n, threads)
+            L.oracle_sum_f64(c.ctypes.data, n, threads)
+            dt = time.perf_counter() - t0
+            best = dt if best is None else min(best, dt)
+        return 12.0 * n / best / 1e9, f"all {n} elements, best of {reps}", best
+
+    res = _baseline("GB/s", "vadd fp32 + fp64 sum loops (test/vadd.vc:40-43, "
+                    "test/reduce.vc:64-75), whole arrays, no extrapolation", measure, 0.0)
+    del a, b, c
+    return res
+
+
+def cpu_baselines(workloads):
+    """CPU baselines for the configurations the bench ran (rank 0, one GPU)."""
+    table = {
+        "gemm": lambda: cpu_gemm_baseline(),
+        "fa_causal": lambda: cpu_attention_baseline(128, 4096, 128, True),
+        "fa_bf16": lambda: cpu_attention_baseline(1024, 8192, 128, False),
+        "stream": lambda: cpu_stream_baseline(),
+        "fa_f32": lambda: cpu_attention_baseline(1, 256, 64, False, target_s=0.5),
+        "gemm_f32": lambda: cpu_gemm_baseline(fp32_inputs=True),
+    }
+    out = {}
+    for name in workloads:
+        if name == "gemm_mblock" and "gemm" in out:
+            out[name] = out["gemm"]  # the same fp64 GEMM loop, per row
+            continue
+        if name == "gemm_mblock":
+            name_fn = table["gemm"]
+            try:
+                out[name] = name_fn()
+            except Exception as e:
+                out[name] = {"error": f"{type(e).__name__}: {e}"}
+            continue
+        if name in table:
+            try:
+                out[name] = table[name]()
+            except Exception as e:  # report, keep the GPU numbers
+                out[name] = {"error": f"{type(e).__name__}: {e}"}
+    return out
+
+
+def reference_arm(args, config):
+    """`--impl reference`: the reference's CPU path for the headline (the fp64
+    GEMM loop of matmul_coopmat_bench.vc:171-176, restated in the oracle), all
+    host threads, on this arm's metric and config. Each step is one bounded
+    sample: `rows` rows of C of one 4096^3 product (about 0.4 s of CPU work);
+    W samples warm up, K are timed, and the value is the K samples' FLOP over
+    their measured time."""
     from oracle import oracle
     N = GEMM_N
     rng = np.random.default_rng(7)
     a = (rng.random((N, N), dtype=np.float32) * 2 - 1).astype(np.float16).astype(np.float32)
     b = (rng.random((N, N), dtype=np.float32) * 2 - 1).astype(np.float16).astype(np.float32)
-    # All host cores this process may run on (torchrun sets OMP_NUM_THREADS=1
-    # for its workers; the baseline overrides it explicitly).
-    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
-    rows = max(2, threads)
+    threads = _cpu_threads()
+    rows, _ = _timed_sample(
+        lambda r: oracle.gemm(a, b, N, N, N, N, N, True, rows=(0, r), threads=threads),
+        max(2, threads), N, 0.4)
+    r0 = [0]
+
+    def sample():
+        lo = r0[0] % (N - rows + 1)
+        oracle.gemm(a, b, N, N, N, N, N, True, rows=(lo, lo + rows), threads=threads)
+        r0[0] += rows
+
+    for _ in range(args.warmup):
+        sample()
     t0 = time.perf_counter()
-    oracle.gemm(a, b, N, N, N, N, N, True, rows=(0, rows), threads=threads)
+    for _ in range(args.steps):
+        sample()
     dt = time.perf_counter() - t0
-    rows2 = int(min(N, max(rows, rows * target_s / max(dt, 1e-3))))
-    t0 = time.perf_counter()
-    oracle.gemm(a, b, N, N, N, N, N, True, rows=(0, rows2), threads=threads)
-    dt2 = time.perf_counter() - t0
-    tflops = 2.0 * rows2 * N * N / dt2 / 1e12
-    return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{rows2} of {N} rows of C = A*B (4096^3 fp16 inputs), fp64 loop "
-                      f"(matmul_coopmat_bench.vc:171-176 form), {dt2:.1f} s",
-            "seconds": round(dt2, 2)}
+    value = 2.0 * rows * N * N * args.steps / dt / 1e12
+    ms = dt / args.steps * 1e3
+    base = {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"each step {rows} of {N} rows of C = A*B (4096^3, fp16 inputs), fp64 loop "
+                      f"(matmul_coopmat_bench.vc:171-176 form); {args.steps} steps timed in "
+                      f"{dt:.2f} s", "seconds": round(dt, 2)}
+    base.update(cpu_info())
+    cfg = {k: v for k, v in config.items() if k not in ("gemms_per_step", "l2")}
+    cfg["step"] = f"one sample: {rows} rows of C of one {N}^3 product"
+    return {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": cfg,
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
 
 
 # ---------------------------------------------------------------- main
@@ -692,7 +992,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default="gemm,fa_causal,fa_bf16,stream,fa_f32,gemm_f32")
+    ap.add_argument("--only", default="gemm,fa_causal,fa_bf16,stream,fa_f32,gemm_f32,gemm_mblock")
     ap.add_argument("--fa-bf16-heads", type=int, default=32,
                     help="heads of the bf16 attention config (32); a smaller count gives a "
                          "launch small enough for an ncu capture, whose DRAM traffic scales "
@@ -713,20 +1013,13 @@ def main():
               "K": GEMM_N, "layout": "row-major A[M][K], B[K][N], C[M][N]",
               "gemms_per_step": GEMMS_PER_STEP,
               "l2": f"inputs rotate over {ROTATE} buffer sets (512 MiB > 126 MB L2)",
-              "parallelism": f"weak: {dist.world} rank(s), one 4096-row block each"}
+              "parallelism": f"weak: {dist.world} rank(s), each the next 4096-row M-block of one "
+                             f"({GEMM_N}*{dist.world}) x {GEMM_N} x {GEMM_N} product, B replicated"}
 
     if args.impl == "reference":
         if dist.rank != 0:
             return
-        base = cpu_gemm_baseline()
-        line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "TFLOP/s",
-                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(2.0 * GEMM_N ** 3 * GEMMS_PER_STEP / (base["value"] * 1e12) * 1e3, 3),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f64", "data": "synthetic", "config": config, "cpu_baseline": base,
-                "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        print(json.dumps(reference_arm(args, config)), flush=True)
         return
 
     import torch
@@ -754,7 +1047,9 @@ def main():
                                               vc.Dtype.F32, max(args.steps, 20), args.warmup, pk,
                                               shard_bh=False)),
             ("gemm_f32", lambda: gemm_f32_workload(vc, dist, max(3, min(args.steps, 10)),
-                                                   args.warmup, pk))]
+                                                   args.warmup, pk)),
+            ("gemm_mblock", lambda: gemm_mblock_workload(vc, dist, max(3, min(args.steps, 10)),
+                                                         args.warmup, pk))]
     for name, fn in jobs:
         if name in only:
             try:
@@ -764,7 +1059,13 @@ def main():
     kerr = vc.kernel_error(True)
 
     if dist.rank == 0:
-        base = cpu_gemm_baseline() if head else None
+        # CPU baselines on one GPU only (rank 0 of a one-rank job).
+        bases = cpu_baselines((["gemm"] if head else []) + [a.get("workload") for a in also]
+                              ) if dist.world == 1 else {}
+        base = bases.get("gemm")
+        for a in also:
+            if a.get("workload") in bases:
+                a["cpu_baseline"] = bases[a["workload"]]
         line = {"metric": METRIC, "value": head["value"] if head else None, "unit": "TFLOP/s",
                 "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": head["ms_per_step"] if head else None,
