@@ -79,6 +79,12 @@ constexpr int kWgThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kBoxBytes = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// P reaches the MMA warp in kHandoffs parts of BKV / kHandoffs keys, each as
+// soon as it is in TMEM, so the PV MMAs of one part overlap the exponentials
+// of the next.
+constexpr int kHandoffs = 2;
+constexpr int kChunksPerHandoff = (BKV / 32) / kHandoffs;  // 32-key chunks per part
+static_assert(kChunksPerHandoff >= 1 && (BKV / 32) % kHandoffs == 0, "hand-off split");
 // Slices per causal ordering group (8 x 16 x 4096 x 128: groups of 4 / 8 /
 // 16 ran 552 / 539 / 542 us; at N = 16384, 932 / 938 / 950 us).
 constexpr int kCausalGroup = 8;
@@ -90,7 +96,7 @@ struct __align__(8) FlashBarriers {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t p_full[2][kHandoffs];  // [tile][part of the keys]
   uint64_t o_full[2];
   uint32_t tmem_base;
 };
@@ -161,7 +167,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
     }
     for (int w = 0; w < 2; ++w) {
       mbar_init(&bars->s_full[w], 1);
-      mbar_init(&bars->p_full[w], kWgThreads / 32);  // one per warp
+      for (int h = 0; h < kHandoffs; ++h)
+        mbar_init(&bars->p_full[w][h], kWgThreads / 32);  // one per warp
       mbar_init(&bars->o_full[w], 1);
     }
     fence_barrier_init();
@@ -217,26 +224,46 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       // ------------------------------------------------ MMA issuer
       const uint32_t idesc_s = idesc_f16_f32(BQ, BKV, BF16, false, false);
       const uint32_t idesc_o = idesc_f16_f32(BQ, HD, BF16, false, true);
-      const uint32_t q0_addr = smem_u32(smem + L::kQ0), q1_addr = smem_u32(smem + L::kQ1);
-      const uint32_t ring = smem_u32(smem + L::kRing);
+      // Descriptors are built once; a byte offset within the shared window
+      // is an add of (offset >> 4) to the descriptor's address field (every
+      // address here is below 256 KiB, so the 14-bit field never carries).
+      // The single issuing thread shares its SM sub-partition with two
+      // softmax warps: every instruction it needs per MMA delays the MMAs.
+      const uint64_t dq0 = smem_desc_sw128(smem_u32(smem + L::kQ0), 16, 1024);
+      const uint64_t dq1 = smem_desc_sw128(smem_u32(smem + L::kQ1), 16, 1024);
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(smem + L::kRing), 16, 1024);
+      const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::kRing), kBoxBytes, 1024);
       auto issue_s = [&](int w, uint32_t k_idx) {
-        const uint32_t kaddr = ring + (k_idx % kStages) * L::kTile;
+        const uint64_t dq = w ? dq1 : dq0;
+        const uint64_t dk = dk0 + (((k_idx % kStages) * L::kTile) >> 4);
+        const uint32_t d_tmem = tmem + w * 128;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t off = (ks / 4) * kBoxBytes + (ks % 4) * 32;
-          mma_f16_ss(tmem + w * 128, smem_desc_sw128((w ? q1_addr : q0_addr) + off, 16, 1024),
-                     smem_desc_sw128(kaddr + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
+          const uint64_t off = (ks / 4) * (kBoxBytes >> 4) + (ks % 4) * (32 >> 4);
+          mma_f16_ss(d_tmem, dq + off, dk + off, idesc_s, ks > 0 ? 1u : 0u);
         }
         mma_commit(&bars->s_full[w]);
       };
-      auto issue_pv = [&](int w, uint32_t v_idx, bool accumulate) {
-        const uint32_t vaddr = ring + (v_idx % kStages) * L::kTile;
+      // O_w += P_w V, part by part (part h: keys h * BKV / kHandoffs ..., in
+      // TMEM columns of P_w from h * 64 / kHandoffs), each part as soon as
+      // its P has landed.
+      auto issue_pv = [&](int w, uint32_t v_idx, bool accumulate, uint32_t parity) {
+        const uint64_t dv = dv0 + (((v_idx % kStages) * L::kTile) >> 4);
+        const uint32_t o_tmem = tmem + 256 + w * 128, p_tmem = tmem + w * 128;
+        constexpr int kSteps = (BKV / 16) / kHandoffs;  // K = 16 MMAs per part
 #pragma unroll
-        for (int ks = 0; ks < BKV / 16; ++ks)
-          mma_f16_ts(tmem + 256 + w * 128, tmem + w * 128 + ks * 8,
-                     smem_desc_sw128(vaddr + ks * 16 * 128, kBoxBytes, 1024), idesc_o,
-                     (accumulate || ks > 0) ? 1u : 0u);
+        for (int h = 0; h < kHandoffs; ++h) {
+          if (!mbar_wait(&bars->p_full[w][h], parity)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kSteps; ++kk) {
+            const int ks = h * kSteps + kk;
+            mma_f16_ts(o_tmem, p_tmem + ks * 8, dv + ks * ((16 * 128) >> 4), idesc_o,
+                       (accumulate || ks > 0) ? 1u : 0u);
+          }
+        }
         mma_commit(&bars->o_full[w]);
+        return true;
       };
       auto wait_full = [&](uint32_t idx) {
         const bool ok = mbar_wait(&bars->kv_full[idx % kStages], (idx / kStages) & 1u);
@@ -254,18 +281,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         if (!wait_full(v_idx)) break;
         bool k_ready = false;
         if (j < n0) {
-          if (!mbar_wait(&bars->p_full[0], j & 1)) break;
-          tc_fence_after();
-          issue_pv(0, v_idx, j > 0);
+          if (!issue_pv(0, v_idx, j > 0, j & 1)) break;
           if (j + 1 < n0) {
             if (!wait_full(k_next)) break;
             k_ready = true;
             issue_s(0, k_next);
           }
         }
-        if (!mbar_wait(&bars->p_full[1], j & 1)) break;
-        tc_fence_after();
-        issue_pv(1, v_idx, j > 0);
+        if (!issue_pv(1, v_idx, j > 0, j & 1)) break;
         mma_commit(&bars->kv_empty[v_idx % kStages]);
         if (j + 1 < n1) {
           if (!k_ready && !wait_full(k_next)) break;
@@ -333,6 +356,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         m_run = m_cand;
       }
       const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+      const bool rescale_o = rescale && j > 0;  // warp-uniform
+      int handed = 0;                           // parts of P handed over
       // P = exp2(scale_log2 * s - m) -> 16-bit pairs over S columns.
       // Two packed (f32x2) partial-sum pairs.
       float lsp[4] = {0.f, 0.f, 0.f, 0.f};
@@ -361,25 +386,34 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             add2(lsp[a], lsp[a + 1], lsp[a], lsp[a + 1], p0, p1);
         }
         tmem_st16(s_col + c * 16, p);
-      }
-      l_run += (lsp[0] + lsp[1]) + (lsp[2] + lsp[3]);
-      if (rescale && j > 0) {
-        // S_w(j) complete implies PV_w(j-1) complete: O_w is stable. Done
-        // after P so that S is no longer live in registers.
+        if (rescale_o && c == 1) {
+          // S_w(j) complete implies PV_w(j-1) complete: O_w is stable, and
+          // no PV_w(j) is issued before the hand-offs below (they wait for
+          // this). Done once the first 64 keys of S are no longer live in
+          // registers.
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_col + c * 32, o);
-          tmem_ld_wait();
+          for (int oc = 0; oc < HD / 32; ++oc) {
+            uint32_t o[32];
+            tmem_ld32(o_col + oc * 32, o);
+            tmem_ld_wait();
 #pragma unroll
-          for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
-          tmem_st32(o_col + c * 32, o);
+            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+            tmem_st32(o_col + oc * 32, o);
+          }
+        }
+        // Hand over every part whose P is complete (with an O rescale
+        // pending, not before it is done).
+        if ((c + 1) % kChunksPerHandoff == 0 && (!rescale_o || c >= 1)) {
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          const int upto = c / kChunksPerHandoff;
+          if (lane == 0)
+            for (int h = handed; h <= upto; ++h) mbar_arrive(&bars->p_full[w][h]);
+          handed = upto + 1;
         }
       }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[w]);
+      l_run += (lsp[0] + lsp[1]) + (lsp[2] + lsp[3]);
       if (!ok) break;
     }
     // Epilogue: O / l -> 16-bit, staged over this tile's Q buffer, TMA store.
