@@ -39,23 +39,23 @@
 // the end of the grid). Non-causal: query blocks of one slice are adjacent.
 // Either way the slices in flight (and their K/V) stay within L2.
 //
-// What bounds it (measured on B200 with clock64 probes): back-to-back
-// tcgen05.mma (M=128, K=16) costs 107 cycles for the S shape (SS, N=128) and
-// 94 for the PV shape (TS, N=128) against 64 at the nominal rate (171 and
-// 138 for N=256; the same per SM for the CTA-pair form; independent of
-// operand layout and data), so a 128-key step of both tiles is >= 3222 MMA
-// cycles; with the softmax removed the kernel runs at that bound, and with
-// it the step measures ~3550 cycles. TMEM is full at d = 128, so neither
-// 256-key S tiles nor Q in TMEM (the cheaper TS form for S) fit. Exponentials
-// on an FMA-pipe polynomial (1/8 .. 1/2 of them) shorten the softmax but slow
-// the concurrent MMAs more (net -1 .. -25 %); two warpgroups taking turns on
-// MUFU measured -1.5 %; a persistent variant (items from an atomic counter,
-// next item's S under the current epilogue) measured -1 % causal, -5 % at
-// N = 16384 causal, +2 % non-causal (traced: each warpgroup still waits for
-// its last PV and runs its own epilogue at every item boundary, and short
-// items bring the two warpgroups into phase on MUFU); issuing the first
-// loads before the CTA-wide barrier, with S0(0) waiting on Q0 alone,
-// measured -1 %.
+// What bounds it (measured on B200 with clock64 probes and in-kernel traces):
+// from a tight single-thread loop every tcgen05.mma shape used here runs at
+// the nominal rate (M=128, K=16: 64 cycles for SS N=128 and TS N=128, 128
+// for SS N=256), so the shapes cap nothing. In this kernel a 128-key step of
+// both tiles takes ~3350 cycles against 2048 of MMA, and the single issuing
+// thread is busy the whole step (it never waits for P: each hand-off has
+// landed by the time it looks); the MMAs are accepted every ~72-77 cycles.
+// Probes put the loss in contention with the rest of the SM: busy warps on
+// the issuer's sub-partition (72 cycles per MMA with FMA-bound neighbours),
+// softmax TMEM loads (75 with continuous loads), the K/V TMA writes (~5 %:
+// the same kernel without refills). Handing P over in two halves, so the
+// first half's PV MMAs run under the second half's exponentials, gave +3.6 %
+// (causal N=4096) to +9 % (N=8192); tried and slower: exponentials partly on
+// an FMA-pipe polynomial (-1 .. -5 %), P in four parts (-3 .. -4 % against
+// halves), one issuing thread per query tile (-15 %: the two tiles' MMAs
+// interleave in the tensor queue and each tile's S finishes later), K and V
+// of a key tile on one barrier (-0.5 %), a persistent grid (-1 .. -5 %).
 // Roofline: 4*BH*N^2*d FLOP (2*BH*N^2*d causal) against the dense tensor peak.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -233,22 +233,25 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       const uint64_t dq1 = smem_desc_sw128(smem_u32(smem + L::kQ1), 16, 1024);
       const uint64_t dk0 = smem_desc_sw128(smem_u32(smem + L::kRing), 16, 1024);
       const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::kRing), kBoxBytes, 1024);
+      const uint32_t dq0_lo = (uint32_t)dq0, dq1_lo = (uint32_t)dq1;
+      const uint32_t dq_hi = (uint32_t)(dq0 >> 32), dk_hi = (uint32_t)(dk0 >> 32);
+      const uint32_t dv_hi = (uint32_t)(dv0 >> 32);
       auto issue_s = [&](int w, uint32_t k_idx) {
-        const uint64_t dq = w ? dq1 : dq0;
-        const uint64_t dk = dk0 + (((k_idx % kStages) * L::kTile) >> 4);
+        const uint32_t q_lo = w ? dq1_lo : dq0_lo;
+        const uint32_t k_lo = (uint32_t)dk0 + (((k_idx % kStages) * L::kTile) >> 4);
         const uint32_t d_tmem = tmem + w * 128;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint64_t off = (ks / 4) * (kBoxBytes >> 4) + (ks % 4) * (32 >> 4);
-          mma_f16_ss(d_tmem, dq + off, dk + off, idesc_s, ks > 0 ? 1u : 0u);
+          const uint32_t off = (ks / 4) * (kBoxBytes >> 4) + (ks % 4) * (32 >> 4);
+          mma_f16_ss_lohi(d_tmem, q_lo + off, dq_hi, k_lo + off, dk_hi, idesc_s, ks > 0 ? 1u : 0u);
         }
         mma_commit(&bars->s_full[w]);
       };
       // O_w += P_w V, part by part (part h: keys h * BKV / kHandoffs ..., in
       // TMEM columns of P_w from h * 64 / kHandoffs), each part as soon as
       // its P has landed.
-      auto issue_pv = [&](int w, uint32_t v_idx, bool accumulate, uint32_t parity) {
-        const uint64_t dv = dv0 + (((v_idx % kStages) * L::kTile) >> 4);
+      auto issue_pv = [&](int w, uint32_t v_idx, bool accumulate, uint32_t parity, bool last) {
+        const uint32_t v_lo = (uint32_t)dv0 + (((v_idx % kStages) * L::kTile) >> 4);
         const uint32_t o_tmem = tmem + 256 + w * 128, p_tmem = tmem + w * 128;
         constexpr int kSteps = (BKV / 16) / kHandoffs;  // K = 16 MMAs per part
 #pragma unroll
@@ -258,11 +261,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
 #pragma unroll
           for (int kk = 0; kk < kSteps; ++kk) {
             const int ks = h * kSteps + kk;
-            mma_f16_ts(o_tmem, p_tmem + ks * 8, dv + ks * ((16 * 128) >> 4), idesc_o,
-                       (accumulate || ks > 0) ? 1u : 0u);
+            mma_f16_ts_lohi(o_tmem, p_tmem + ks * 8, v_lo + ks * ((16 * 128) >> 4), dv_hi,
+                            idesc_o, (accumulate || ks > 0) ? 1u : 0u);
           }
         }
-        mma_commit(&bars->o_full[w]);
+        // Only the epilogue waits for O: one commit after the tile's last PV.
+        if (last) mma_commit(&bars->o_full[w]);
         return true;
       };
       auto wait_full = [&](uint32_t idx) {
@@ -281,14 +285,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         if (!wait_full(v_idx)) break;
         bool k_ready = false;
         if (j < n0) {
-          if (!issue_pv(0, v_idx, j > 0, j & 1)) break;
+          if (!issue_pv(0, v_idx, j > 0, j & 1, j + 1 == n0)) break;
           if (j + 1 < n0) {
             if (!wait_full(k_next)) break;
             k_ready = true;
             issue_s(0, k_next);
           }
         }
-        if (!issue_pv(1, v_idx, j > 0, j & 1)) break;
+        if (!issue_pv(1, v_idx, j > 0, j & 1, j + 1 == n1)) break;
         mma_commit(&bars->kv_empty[v_idx % kStages]);
         if (j + 1 < n1) {
           if (!k_ready && !wait_full(k_next)) break;
@@ -417,7 +421,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       if (!ok) break;
     }
     // Epilogue: O / l -> 16-bit, staged over this tile's Q buffer, TMA store.
-    if (__all_sync(0xffffffffu, ok && nkv > 0 && mbar_wait(&bars->o_full[w], (nkv - 1) & 1))) {
+    if (__all_sync(0xffffffffu, ok && nkv > 0 && mbar_wait(&bars->o_full[w], 0))) {
       tc_fence_after();
       uint8_t *stage = smem + (w ? L::kQ1 : L::kQ0);
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;

@@ -78,13 +78,29 @@ __device__ __forceinline__ bool mbar_test_parity(uint32_t bar_addr,
   return done != 0;
 }
 
+// Non-blocking test of the same (mbarrier.test_wait). Measured on B200: an
+// MMA-issuing thread that checks an already completed phase with try_wait
+// after tcgen05.commit stalls the tensor pipe ~73 cycles per check, with
+// test_wait ~26; so waits test first and suspend only when they must.
+__device__ __forceinline__ bool mbar_test_nb(uint32_t bar_addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Wait for the completion of the barrier phase whose parity is `parity`.
 // Bounded by `limit_ns` of wall time; false (and an error recorded) on
 // timeout. `limit_ns` defaults to 4 s, far above any legitimate wait here.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
                                           uint64_t limit_ns = 4000000000ull) {
   const uint32_t addr = smem_u32(bar);
-  if (mbar_test_parity(addr, parity)) return true;
+  if (mbar_test_nb(addr, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_test_parity(addr, parity)) return true;
@@ -111,7 +127,15 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
         : "memory");
     return done != 0;
   };
-  if (test()) return true;
+  uint32_t first;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(first)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  if (first) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t spin = 1;; ++spin) {
     if (test()) return true;
@@ -285,6 +309,34 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem,
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The same two MMA forms with each shared-memory descriptor passed as its two
+// 32-bit halves: advancing a descriptor within the shared window only changes
+// the address field of the low word, so a loop that steps through operand
+// tiles adds to one 32-bit register per operand and keeps the high words
+// invariant (fewer instructions on the issuing thread per MMA).
+__device__ __forceinline__ void mma_f16_ss_lohi(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
+                                                uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "mov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16_ts_lohi(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
+                                                uint32_t b_hi, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
