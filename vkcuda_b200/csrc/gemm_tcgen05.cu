@@ -310,6 +310,7 @@ constexpr size_t kPairSmemBytes =
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmBh,
                          const __grid_constant__ CUtensorMap tmD,
                          const float *__restrict__ Cin, int64_t ldc, int M, int N, int K,
                          uint32_t idesc_full, uint32_t idesc_half, int b_kn, int num_full,
@@ -364,6 +365,7 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmBh);
     tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
@@ -393,18 +395,24 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         unit_tile(u, tm, n0, width);
         const int a_row = tm * 2 * BM + rank * BM;
         const int b_col = n0 + rank * (width / 2);
+        // A half unit (N = 128 per pair) needs 64 columns of B per CTA: it
+        // loads only those, so its stages carry 24 KiB per CTA instead of 32
+        // (loading the full 128 made the tail's half units as slow as full
+        // tiles: the stage copies, not the MMAs, set their pace).
+        const bool half = width < BN;
+        const uint32_t stage_bytes = kPairABytes + (half ? kPairBBytes / 2 : kPairBBytes);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1u)) { ok = false; break; }
           uint8_t *sA = stage_base + stage * kPairStageBytes;
           uint8_t *sB = sA + kPairABytes;
-          if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * kPairStageBytes);
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * stage_bytes);
           const uint32_t fb = lead(&bars->full[stage]);
           tma_load_2d_pair(sA, &tmA, kb * BK, a_row, fb);
           if (b_kn) {
             tma_load_2d_pair(sB, &tmB, b_col, kb * BK, fb);
-            tma_load_2d_pair(sB + 64 * BK * 2, &tmB, b_col + 64, kb * BK, fb);
+            if (!half) tma_load_2d_pair(sB + 64 * BK * 2, &tmB, b_col + 64, kb * BK, fb);
           } else {
-            tma_load_2d_pair(sB, &tmB, kb * BK, b_col, fb);
+            tma_load_2d_pair(sB, half ? &tmBh : &tmB, kb * BK, b_col, fb);
           }
           ++issued;
           if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
@@ -533,7 +541,7 @@ namespace {
 struct MapCache {
   GemmArgs key{};
   int device = -1;
-  CUtensorMap a, b, b_pair, d;
+  CUtensorMap a, b, b_pair, b_pair_half, d;
   bool valid = false;
 };
 
@@ -586,9 +594,11 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
     if (g.b_kn) {
       ok = ok && make_map_2d(&cache.b, t16, 2, g.B, g.N, g.K, g.ldb, 64, BK);
       cache.b_pair = cache.b;
+      cache.b_pair_half = cache.b;
     } else {
       ok = ok && make_map_2d(&cache.b, t16, 2, g.B, g.K, g.N, g.ldb, BK, BN);
       ok = ok && make_map_2d(&cache.b_pair, t16, 2, g.B, g.K, g.N, g.ldb, BK, BN / 2);
+      ok = ok && make_map_2d(&cache.b_pair_half, t16, 2, g.B, g.K, g.N, g.ldb, BK, BN / 4);
     }
     ok = ok && make_map_2d(&cache.d, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.D, g.N, g.M,
                            g.ldd, kEpiCols, 32);
@@ -643,7 +653,8 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs &g, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_tcgen05_pair_kernel, cache.a, cache.b_pair, cache.d,
+    return cudaLaunchKernelEx(&cfg, gemm_tcgen05_pair_kernel, cache.a, cache.b_pair,
+                              cache.b_pair_half, cache.d,
                               g.Cin, g.ldc, g.M, g.N, g.K, idesc_full, idesc_half,
                               g.b_kn ? 1 : 0, num_full, num_units,
                               (size_t)g.K * (size_t)g.N * 2 > kGroupAboveBBytes ? kGroupRows : 1);
