@@ -183,8 +183,8 @@ int vc_sum_f32(const float *x, int64_t n, double *out, void *stream);
  * library (1024 partial slots; a device that would need more blocks is
  * refused with VC_INVALID_VALUE). All calls share that array: calls that
  * overlap on the GPU race. The first call on a device looks up the array's
- * address; make it before any stream capture. Uses the calling thread's
- * current CUDA device. */
+ * address; make it before any stream capture. Runs on the runtime's current
+ * device (vc_set_device), as vc_sum_f32 does. */
 int vc_sum_f32_noalloc(const float *x, int64_t n, double *out, void *stream);
 
 /* Fused: c = a + b and *out = sum(c) in one pass (12 bytes per element). */
