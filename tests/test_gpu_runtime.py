@@ -254,3 +254,47 @@ def test_multigpu_demo_semantics(gpu, dev):
     assert np.array_equal(back, (2000 + np.arange(count)).astype(np.float32))
     assert gpu.vcSetDevice(0) == 0
     assert gpu.vcFree(dst) == 0 and gpu.vcFree(two) == 0      # device-1 buffers, device 0 current
+
+
+def test_poison_fill_outputs(gpu):
+    """VC_POISON=1 (the NaN-canary debug aid that stands in for an
+    initialisation checker): every launch first fills the region its kernel's
+    contract says it writes with 0xFF bytes, so a skipped element would read
+    back NaN. Kernels that write their whole output give unchanged results;
+    an in-place call (output sharing memory with an input) is not poisoned."""
+    r = _child("from vkcuda_b200 import vc\n"
+               "import numpy as np\n"
+               "assert vc.vcInit() == 0\n"
+               "n = 1000\n"
+               "a = np.arange(n, dtype=np.float32); b = np.full(n, 2.0, np.float32)\n"
+               "e, da = vc.vcMalloc(4 * n); e, db = vc.vcMalloc(4 * n); e, dc = vc.vcMalloc(4 * n)\n"
+               "assert vc.vcMemcpy(da, a, 4 * n, vc.VCMemcpyKind.HostToDevice) == 0\n"
+               "assert vc.vcMemcpy(db, b, 4 * n, vc.VCMemcpyKind.HostToDevice) == 0\n"
+               "e, k = vc.vcGetKernel('vadd')\n"
+               "assert vc.vcLaunchKernel(k, n, 32, [vc.ptr(da), vc.ptr(db), vc.ptr(dc), vc.i32(n)]) == 0\n"
+               "c = np.empty(n, np.float32)\n"
+               "assert vc.vcMemcpy(c, dc, 4 * n, vc.VCMemcpyKind.DeviceToHost) == 0\n"
+               "assert np.array_equal(c, a + b)\n"
+               "import sys; print('INPLACE', file=sys.stderr, flush=True)\n"
+               "assert vc.vcLaunchKernel(k, n, 32, [vc.ptr(da), vc.ptr(db), vc.ptr(da), vc.i32(n)]) == 0\n"
+               "assert vc.vcMemcpy(c, da, 4 * n, vc.VCMemcpyKind.DeviceToHost) == 0\n"
+               "assert np.array_equal(c, a + b)\n"
+               "print('GEMM', file=sys.stderr, flush=True)\n"
+               "M = N = K = 256\n"
+               "A = (np.arange(M * K) % 7).astype(np.float16); B = (np.arange(K * N) % 5).astype(np.float16)\n"
+               "e, dA = vc.vcMalloc(2 * M * K); e, dB = vc.vcMalloc(2 * K * N); e, dD = vc.vcMalloc(4 * M * N)\n"
+               "assert vc.vcMemcpy(dA, A, A.nbytes, vc.VCMemcpyKind.HostToDevice) == 0\n"
+               "assert vc.vcMemcpy(dB, B, B.nbytes, vc.VCMemcpyKind.HostToDevice) == 0\n"
+               "assert vc.gemm(dA, dB, dD, None, M, N, K, K, N, N, 0, vc.Dtype.F16, True) == 0\n"
+               "D = np.empty(M * N, np.float32)\n"
+               "assert vc.vcMemcpy(D, dD, D.nbytes, vc.VCMemcpyKind.DeviceToHost) == 0\n"
+               "ref = A.astype(np.float64).reshape(M, K) @ B.astype(np.float64).reshape(K, N)\n"
+               "assert np.array_equal(D.reshape(M, N), ref)\n"
+               "assert vc.vcShutdown() == 0\n",
+               {"VC_POISON": "1", "VC_DEBUG": "1"})
+    assert r.returncode == 0, r.stderr
+    before, _, rest = r.stderr.partition("INPLACE")
+    inplace, _, gemm = rest.partition("GEMM")
+    assert "vc: poison vadd output" in before
+    assert "vc: poison vadd output" not in inplace      # c shares memory with a
+    assert "vc: poison vc.gemm output" in gemm and "256 x 1024 bytes" in gemm

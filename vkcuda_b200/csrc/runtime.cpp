@@ -20,7 +20,8 @@
 //     worker thread, so the callback may call back into the runtime as the
 //     reference allows (VCRuntime.h:536-542).
 // Environment: VC_PROFILE=1 (per-op GPU timings, table at vcShutdown),
-// VC_DEBUG=1 (diagnostics), VC_SYNC_TIMEOUT_MS=<ms> (bounded host waits that
+// VC_DEBUG=1 (diagnostics), VC_POISON=1 (outputs filled with NaN canaries
+// before each registry launch), VC_SYNC_TIMEOUT_MS=<ms> (bounded host waits that
 // return NotReady), VC_FAULT_INJECT=malloc:N,launch:N,memcpy:N (the Nth call
 // of that kind fails, for host-side failure tests).
 #include <cuda.h>
@@ -34,6 +35,7 @@
 #include <cstring>
 #include <deque>
 #include <fstream>
+#include <initializer_list>
 #include <map>
 #include <mutex>
 #include <string>
@@ -113,6 +115,7 @@ struct State {
   bool printf_flag = false;
   bool profile = false;
   bool debug = false;
+  bool poison = false;  // VC_POISON=1: NaN canaries in outputs before launches
   long sync_timeout_ms = 0;
   std::map<uintptr_t, AllocInfo> allocs;
   std::unordered_map<void *, int> stream_device;
@@ -383,6 +386,7 @@ VCError vcInit() {
   S.device_count = n;
   S.profile = std::getenv("VC_PROFILE") && std::atoi(std::getenv("VC_PROFILE")) != 0;
   S.debug = std::getenv("VC_DEBUG") && std::atoi(std::getenv("VC_DEBUG")) != 0;
+  S.poison = std::getenv("VC_POISON") && std::atoi(std::getenv("VC_POISON")) != 0;
   S.sync_timeout_ms = std::getenv("VC_SYNC_TIMEOUT_MS") ? std::atol(std::getenv("VC_SYNC_TIMEOUT_MS")) : 0;
   parse_faults_locked(S);
   S.initialized = true;
@@ -1077,6 +1081,43 @@ long long konst(const VCKernel &k, const char *name) {
 
 VCError run(cudaError_t e, const char *what) { return map_cuda(e, what); }
 
+// ---- VC_POISON=1: a NaN canary in every output before its kernel runs.
+// With compute-sanitizer closed, this is how a kernel that leaves part of its
+// output unwritten shows itself: the region the kernel's contract says it
+// writes is filled with 0xFF bytes (NaN for fp32 / fp16 / bf16, -1 for
+// integers) on the launch stream, so an element the kernel skips reads back
+// as NaN instead of a stale plausible value. A region that shares memory with
+// an input of the same launch (an in-place call) is left alone.
+struct Span {
+  const void *p;
+  size_t bytes;
+};
+bool spans_overlap(const void *p, size_t bytes, std::initializer_list<Span> inputs) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(p), a1 = a0 + bytes;
+  for (const Span &in : inputs) {
+    if (!in.p || !in.bytes) continue;
+    const uintptr_t b0 = reinterpret_cast<uintptr_t>(in.p), b1 = b0 + in.bytes;
+    if (a0 < b1 && b0 < a1) return true;
+  }
+  return false;
+}
+// Output of `rows` rows of `width` bytes, `pitch` bytes apart.
+void poison_output(const char *kernel, void *p, size_t pitch, size_t width, size_t rows,
+                   cudaStream_t s, std::initializer_list<Span> inputs) {
+  if (!st().poison || !p || !width || !rows) return;
+  const size_t span = (rows - 1) * pitch + width;
+  if (spans_overlap(p, span, inputs)) return;
+  cudaError_t e = rows == 1 ? cudaMemsetAsync(p, 0xFF, width, s)
+                            : cudaMemset2DAsync(p, pitch, 0xFF, width, rows, s);
+  if (st().debug)
+    std::fprintf(stderr, "vc: poison %s output %p, %zu x %zu bytes (%s)\n", kernel, p, rows, width,
+                 cudaGetErrorString(e));
+}
+void poison_output(const char *kernel, void *p, size_t bytes, cudaStream_t s,
+                   std::initializer_list<Span> inputs) {
+  poison_output(kernel, p, bytes, bytes, 1, s, inputs);
+}
+
 // vadd(a, b, c, int n): c[i] = a[i] + b[i] for i < min(n, workgroups*block)
 // (test/vadd.vc:12-17).
 VCError k_vadd(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, int n, cudaStream_t s) {
@@ -1091,6 +1132,7 @@ VCError k_vadd(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, int n, c
   const size_t bytes = (size_t)m * 4;
   if (bytes > bytes_available(pa) || bytes > bytes_available(pb) || bytes > bytes_available(pc))
     return too_small("vadd");
+  poison_output("vadd", const_cast<void *>(pc), bytes, s, {{pa, bytes}, {pb, bytes}});
   return run(vcb::launch_vadd_f32((const float *)pa, (const float *)pb, (float *)pc, m, s), "vadd");
 }
 
@@ -1106,6 +1148,7 @@ VCError k_fill_pattern(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, 
   long long m = cnt < covered ? cnt : covered;
   if (m <= 0) return VCError::Success;
   if ((size_t)m * 4 > bytes_available(pa)) return too_small("fillPattern");
+  poison_output("fillPattern", const_cast<void *>(pa), (size_t)m * 4, s, {});
   return run(vcb::launch_fill_pattern((int *)pa, (int)base, m, s), "fillPattern");
 }
 
@@ -1121,6 +1164,8 @@ VCError k_block_reduce(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, 
   if ((size_t)groups * 4 > bytes_available(pout)) return too_small("blockReduce");
   long long need = N < groups * (long long)sh.bx ? N : groups * (long long)sh.bx;
   if (need > 0 && (size_t)need * 4 > bytes_available(pin)) return too_small("blockReduce");
+  poison_output("blockReduce", const_cast<void *>(pout), (size_t)groups * 4, s,
+                {{pin, need > 0 ? (size_t)need * 4 : 0}});
   return run(vcb::launch_block_reduce_demo((const float *)pin, (float *)pout, (int)N, (int)sh.bx,
                                            (int)groups, s), "blockReduce");
 }
@@ -1148,10 +1193,22 @@ VCError k_flash_attn(VCKernel &k, const LaunchShape &sh, const VCKernelArg *a, i
     if (bytes > bytes_available(p)) return too_small("flashAttn");
   vcb::FlashArgs f{q, kk, v, const_cast<void *>(o), (int)nhead, (int)seq, (int)hdim, scale,
                    causal == 1, 0};
+  poison_output("flashAttn", const_cast<void *>(o), bytes, s, {{q, bytes}, {kk, bytes}, {v, bytes}});
   return run(vcb::launch_flash_fwd_f32(f, s), "flashAttn");
 }
 
+// D of a GEMM: M rows of N fp32 at row stride ldd (A, B, Cin are inputs).
+void poison_gemm_output(const vcb::GemmArgs &g, size_t in_esz, cudaStream_t s, const char *name) {
+  const size_t a_span = ((size_t)(g.M - 1) * g.lda + g.K) * in_esz;
+  const size_t b_span = g.b_kn ? ((size_t)(g.K - 1) * g.ldb + g.N) * in_esz
+                               : ((size_t)(g.N - 1) * g.ldb + g.K) * in_esz;
+  const size_t c_span = g.Cin ? ((size_t)(g.M - 1) * g.ldc + g.N) * 4 : 0;
+  poison_output(name, g.D, (size_t)g.ldd * 4, (size_t)g.N * 4, (size_t)g.M, s,
+                {{g.A, a_span}, {g.B, b_span}, {g.Cin, c_span}});
+}
+
 VCError gemm_dispatch(const vcb::GemmArgs &g, cudaStream_t s, const char *name) {
+  poison_gemm_output(g, 2, s, name);
   cudaError_t e = vcb::launch_gemm_tcgen05(g, s);
   if (e == cudaErrorNotSupported) {
     cudaGetLastError();
@@ -1163,6 +1220,7 @@ VCError gemm_dispatch(const vcb::GemmArgs &g, cudaStream_t s, const char *name) 
 // fp32 A, B: the tensor-core path (three tf32 products per product) when
 // TMA can take the strides, else the CUDA-core path.
 VCError gemm_f32_dispatch(const vcb::GemmArgs &g, cudaStream_t s, const char *name) {
+  poison_gemm_output(g, 4, s, name);
   cudaError_t e = vcb::launch_gemm_f32_tcgen05(g, s);
   if (e == cudaErrorNotSupported) {
     cudaGetLastError();
@@ -1240,6 +1298,7 @@ VCError k_native_vadd(VCKernel &, const LaunchShape &, const VCKernelArg *a, int
   const size_t bytes = (size_t)cnt * 4;
   if (bytes > bytes_available(pa) || bytes > bytes_available(pb) || bytes > bytes_available(pc))
     return too_small("vc.vadd");
+  poison_output("vc.vadd", const_cast<void *>(pc), bytes, s, {{pa, bytes}, {pb, bytes}});
   return run(vcb::launch_vadd_f32((const float *)pa, (const float *)pb, (float *)pc, cnt, s), "vc.vadd");
 }
 
@@ -1250,6 +1309,9 @@ VCError sum_common(const float *x, const float *b, float *c, long long cnt, doub
   int cap;
   cudaError_t e = vcb::reduce_scratch(s, &partials, &ticket, &cap);
   if (e != cudaSuccess) return run(e, name);
+  const size_t bytes = (size_t)cnt * 4;
+  poison_output(name, out, 8, s, {{x, bytes}, {b, b ? bytes : 0}, {c, c ? bytes : 0}});
+  if (c) poison_output(name, c, bytes, s, {{x, bytes}, {b, bytes}});
   return run(vcb::launch_sum_f32(x, b, c, cnt, out, partials, ticket, cap, s), name);
 }
 
@@ -1287,6 +1349,8 @@ VCError k_native_block_reduce(VCKernel &, const LaunchShape &, const VCKernelArg
     return bad_args("vc.block_reduce");
   if (block <= 0 || block > 1024 || groups <= 0) return bad_args("vc.block_reduce");
   if ((size_t)groups * 4 > bytes_available(pout)) return too_small("vc.block_reduce");
+  poison_output("vc.block_reduce", const_cast<void *>(pout), (size_t)groups * 4, s,
+                {{pin, N > 0 ? (size_t)N * 4 : 0}});
   return run(vcb::launch_block_reduce_demo((const float *)pin, (float *)pout, (int)N, (int)block,
                                            (int)groups, s), "vc.block_reduce");
 }
@@ -1330,6 +1394,7 @@ VCError flash_checked(const vcb::FlashArgs &f, cudaStream_t s) {
   const size_t bytes = (size_t)f.BH * f.N * f.d * esz;
   for (const void *p : {f.Q, f.K, f.V, (const void *)f.O})
     if (!p || bytes > bytes_available(p)) return too_small("vc.flash_fwd");
+  poison_output("vc.flash_fwd", f.O, bytes, s, {{f.Q, bytes}, {f.K, bytes}, {f.V, bytes}});
   if (f.dtype == VC_DTYPE_F32) return run(vcb::launch_flash_fwd_f32(f, s), "vc.flash_fwd");
   if (f.dtype == VC_DTYPE_F16 || f.dtype == VC_DTYPE_BF16)
     return run(vcb::launch_flash_fwd_tcgen05(f, s), "vc.flash_fwd");
@@ -1727,6 +1792,8 @@ int vc_vadd_f32(const float *a, const float *b, float *c, int64_t n, void *s) {
   if (!a || !b || !c || n < 0) return E(VCError::InvalidValue);
   if (!ensure_init()) return E(VCError::InitializationError);
   use_current_device();
+  const size_t bytes = (size_t)n * 4;
+  poison_output("vc_vadd_f32", c, bytes, reinterpret_cast<cudaStream_t>(s), {{a, bytes}, {b, bytes}});
   return E(map_cuda(vcb::launch_vadd_f32(a, b, c, n, reinterpret_cast<cudaStream_t>(s)), "vc_vadd_f32"));
 }
 int vc_sum_f32(const float *x, int64_t n, double *out, void *s) {
@@ -1830,6 +1897,8 @@ int vc_block_reduce_f32(const float *in, float *out, int n, int block, int group
   if (!in || !out || n < 0 || block <= 0 || block > 1024 || groups <= 0) return E(VCError::InvalidValue);
   if (!ensure_init()) return E(VCError::InitializationError);
   use_current_device();
+  poison_output("vc_block_reduce_f32", out, (size_t)groups * 4, reinterpret_cast<cudaStream_t>(s),
+                {{in, (size_t)n * 4}});
   return E(map_cuda(vcb::launch_block_reduce_demo(in, out, n, block, groups,
                                                   reinterpret_cast<cudaStream_t>(s)),
                     "vc_block_reduce_f32"));
