@@ -6,8 +6,9 @@
 //
 // Layout and roofline: flat fp32 arrays in HBM. The vector kernels move
 // 16-byte vectors with streaming cache hints, keep 4 vectors per operand in
-// flight per thread, and run a grid of (resident CTAs x 148 SMs) so every SM
-// has enough bytes in flight to cover HBM latency. Algorithmic traffic:
+// flight per thread, and run one wave of resident CTAs on every SM (3 per SM
+// at their 40 registers a thread) so every SM has enough bytes in flight to
+// cover HBM latency. Algorithmic traffic:
 // vadd 12 B/elem, sum 4 B/elem, vadd_sum 12 B/elem.
 //
 // Summation order: each thread adds runs of up to 16 elements in fp32 and
@@ -267,17 +268,48 @@ __global__ void fill_pattern_kernel(int *__restrict__ a, int base, int64_t n) {
     a[i] = base + static_cast<int>(i);
 }
 
+int resident_per_sm();
+
 int stream_grid(int64_t work_items) {
   const int sm_count = sm_count_current();
-  // Four resident 512-thread CTAs per SM (2048 threads) keep ~128 KiB in
-  // flight per SM; fewer CTAs when the array is small.
-  const int64_t full = static_cast<int64_t>(sm_count) * 4;
+  // One wave of resident 512-thread CTAs (the grid-stride loops then keep
+  // every SM streaming to the end; a partial second wave measured 2-8 %
+  // slower: 3 vs 4 CTAs per SM at 40 registers a thread); fewer CTAs when
+  // the array is small.
+  const int64_t full = static_cast<int64_t>(sm_count) * resident_per_sm();
   const int64_t need = (work_items + kStreamThreads - 1) / kStreamThreads;
   int64_t g = need < full ? need : full;
   return g < 1 ? 1 : static_cast<int>(g);
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 512-thread CTAs of the streaming kernels that fit on one SM at once (the
+// least over the vector kernels, which share one grid size), per device.
+int resident_per_sm() {
+  constexpr int kMaxDevices = 64;
+  static int by_device[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 3;
+  int *slot = (dev >= 0 && dev < kMaxDevices) ? &by_device[dev] : nullptr;
+  int r = slot ? __atomic_load_n(slot, __ATOMIC_RELAXED) : 0;
+  if (r <= 0) {
+    r = 4;
+    int k = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, vadd_vec_kernel, kStreamThreads, 0) ==
+            cudaSuccess && k > 0)
+      r = k < r ? k : r;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, sum_vec_kernel<true>, kStreamThreads,
+                                                      0) == cudaSuccess && k > 0)
+      r = k < r ? k : r;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, sum_vec_kernel<false>, kStreamThreads,
+                                                      0) == cudaSuccess && k > 0)
+      r = k < r ? k : r;
+    cudaGetLastError();
+    if (slot) __atomic_store_n(slot, r, __ATOMIC_RELAXED);
+  }
+  return r;
+}
 
 }  // namespace
 
@@ -391,8 +423,8 @@ cudaError_t launch_block_reduce_demo(const float *in, float *out, int n, int blo
 // The array below exists once per GPU that loads the library and stays
 // resident until the process exits. It holds kNoAllocMaxPartials block
 // partials (8 KiB) plus the ticket counter, which bounds the grid to 1024
-// blocks; the grid is the same one vc_sum_f32 uses (4 blocks per SM at most,
-// 592 on a B200), so both entries add the same partials in the same order.
+// blocks; the grid is the same one vc_sum_f32 uses (one wave of resident CTAs,
+// 444 on a B200), so both entries add the same partials in the same order.
 // A device that would need more blocks than that is refused with an error.
 // Every call shares the array and it keeps the last call's contents: the
 // ticket is cleared on the stream before each launch (the partial slots are
