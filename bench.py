@@ -98,7 +98,10 @@ def stream_traffic(n):
 
 
 class ClockSampler:
-    """nvidia-smi samples (every 50 ms) while the timed region runs."""
+    """nvidia-smi samples (every 50 ms), each stamped on arrival; started before
+    the idle period and the warm-up (nvidia-smi takes a moment to produce its
+    first line), summarised over the samples that arrived inside the timed
+    window `window` = (t0, t1) of time.monotonic()."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -108,6 +111,7 @@ class ClockSampler:
         self.uuid = device_uuid
         self.proc = None
         self.lines = []
+        self.window = None
 
     def __enter__(self):
         try:
@@ -123,7 +127,7 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
     def __exit__(self, *exc):
         if self.proc:
@@ -136,7 +140,12 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        lines = list(self.lines)
+        if self.window is not None:
+            t0, t1 = self.window
+            # a sample arriving up to one period after the window describes it
+            lines = [(t, l) for t, l in lines if t0 <= t <= t1 + 0.05]
+        for _, line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 7:
                 continue
@@ -211,21 +220,25 @@ def timed(dist, stream, fn, steps, warmup, sampler=None, stats=None):
     max over ranks, in ms. With `stats` (a dict), an event between steps also
     gives this rank's median and best step time (`median_ms`, `best_ms`)."""
     import torch
-    torch.cuda.synchronize()
-    time.sleep(IDLE_BEFORE_S)
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    events = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     ctx = sampler if sampler is not None else _Null()
     with ctx:
+        torch.cuda.synchronize()
+        time.sleep(IDLE_BEFORE_S)
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        t0 = time.monotonic()
         events[0].record(stream)
         for i in range(steps):
             fn()
             events[i + 1].record(stream)
         torch.cuda.synchronize()
+        t1 = time.monotonic()
+    if sampler is not None:
+        sampler.window = (t0, t1)
     dist.barrier()
     if stats is not None:
         per = [events[i].elapsed_time(events[i + 1]) for i in range(steps)]
