@@ -139,3 +139,48 @@ def spirv_module(entry: str) -> list:
     words += [(3 << 16) | 14, 0, 1]                      # OpMemoryModel Logical GLSL450
     words += [((3 + len(name_words)) << 16) | 15, 5, 1] + name_words  # OpEntryPoint GLCompute %1
     return words
+
+
+def spirv_glsl_module(buffers, push) -> list:
+    """Words of a SPIR-V module shaped like the VC compiler's GLSL backend
+    output for one kernel (lib/Codegen/ASTToGLSL.cpp:955-1008 in the
+    reference): entry "main"; one storage-buffer block per pointer parameter,
+    `buffer Bi { T name[]; }` at binding i; one push-constant block with the
+    scalar parameters in order. `buffers` and `push` are lists of (name,
+    "f32" | "i32"). Only the instructions a loader reads are emitted."""
+    def lit(text):
+        b = text.encode() + b"\0"
+        b += b"\0" * (-len(b) % 4)
+        return [int.from_bytes(b[i:i + 4], "little") for i in range(0, len(b), 4)]
+
+    def ins(op, *operands):
+        return [((1 + len(operands)) << 16) | op, *operands]
+
+    ids = iter(range(1, 1000))
+    main, f32, i32 = next(ids), next(ids), next(ids)
+    words = ins(17, 1) + ins(14, 0, 1) + ins(15, 5, main, *lit("main"))
+    words += ins(22, f32, 32) + ins(21, i32, 32, 1)
+    tid = {"f32": f32, "i32": i32}
+    for b, (name, ty) in enumerate(buffers):
+        rt, st, ptr, var = next(ids), next(ids), next(ids), next(ids)
+        words += ins(29, rt, tid[ty]) + ins(30, st, rt)
+        words += ins(5, st, *lit(f"B{b}")) + ins(6, st, 0, *lit(name)) + ins(71, st, 2)
+        words += ins(32, ptr, 12, st) + ins(59, ptr, var, 12)
+        words += ins(71, var, 34, 0) + ins(71, var, 33, b)
+    if push:
+        st, ptr, var = next(ids), next(ids), next(ids)
+        words += ins(30, st, *[tid[ty] for _, ty in push]) + ins(5, st, *lit("PC"))
+        for m, (name, _) in enumerate(push):
+            words += ins(6, st, m, *lit(name))
+        words += ins(32, ptr, 9, st) + ins(59, ptr, var, 9)
+    return [0x07230203, 0x00010000, 0, 1000, 0] + words
+
+
+GLSL_DEMO_INTERFACES = {
+    "vadd": ([("a", "f32"), ("b", "f32"), ("c", "f32")], [("n", "i32")]),
+    "blockReduce": ([("inBuf", "f32"), ("outBuf", "f32")], [("N", "i32")]),
+    "flashAttn": ([("Q", "f32"), ("K", "f32"), ("V", "f32"), ("O", "f32")],
+                  [("scale", "f32"), ("causal", "i32")]),
+    "matmulTiled": ([("A", "f32"), ("B", "f32"), ("C", "f32")], [("N", "i32")]),
+    "fillPattern": ([("a", "i32")], [("base", "i32"), ("n", "i32")]),
+}

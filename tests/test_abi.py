@@ -10,7 +10,7 @@ import sys
 
 import pytest
 
-from conftest import spirv_module
+from conftest import GLSL_DEMO_INTERFACES, spirv_glsl_module, spirv_module
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -73,7 +73,7 @@ def test_no_device_behaviour(vc):
 
 def test_kernel_registry_host_logic(vc):
     for name in ["flashAttn", "wmma_gemm", "matmulCoopmat", "matmulTiled", "vadd", "blockReduce",
-                 "fillPattern",
+                 "fillPattern", "matmul",
                  "vc.gemm", "vc.flash_fwd", "vc.vadd", "vc.sum", "vc.vadd_sum",
                  "vc.block_reduce"]:
         err, k = vc.vcGetKernel(name)
@@ -100,6 +100,37 @@ def test_kernel_registry_host_logic(vc):
     assert vc.vcKernelSetConstant(k, "NOPE", 1) == vc.VCError.InvalidValue
     assert vc.vcKernelSetConstant(k, "SEQ", 0) == vc.VCError.InvalidValue
     vc.vcReleaseKernel(k)
+
+
+def test_glsl_backend_modules_resolve_by_interface(vc):
+    """A GLSL-backend module names its entry "main"; its storage-buffer and
+    push-constant member names and types identify the demo kernel."""
+    for name, (bufs, push) in GLSL_DEMO_INTERFACES.items():
+        err, k = vc.vcLoadKernel(spirv_glsl_module(bufs, push), "main")
+        assert err == vc.VCError.Success and k, name
+        vc.vcReleaseKernel(k)
+    # Another kernel's interface (a renamed parameter, a wrong element type,
+    # a missing scalar) is not taken for a demo kernel.
+    assert vc.vcLoadKernel(spirv_glsl_module([("x", "f32"), ("b", "f32"), ("c", "f32")],
+                                             [("n", "i32")]), "main")[0] == vc.VCError.InvalidKernel
+    assert vc.vcLoadKernel(spirv_glsl_module([("a", "i32"), ("b", "f32"), ("c", "f32")],
+                                             [("n", "i32")]), "main")[0] == vc.VCError.InvalidKernel
+    assert vc.vcLoadKernel(spirv_glsl_module([("a", "f32"), ("b", "f32"), ("c", "f32")], []),
+                           "main")[0] == vc.VCError.InvalidKernel
+
+
+def test_glsl_backend_module_identity_is_reported():
+    out = subprocess.run(
+        [sys.executable, "-c",
+         "import sys; sys.path.insert(0, 'tests')\n"
+         "from conftest import GLSL_DEMO_INTERFACES, spirv_glsl_module\n"
+         "from vkcuda_b200 import vc\n"
+         "b, p = GLSL_DEMO_INTERFACES['blockReduce']\n"
+         "print(int(vc.vcLoadKernel(spirv_glsl_module(b, p), 'main')[0]))\n"],
+        capture_output=True, text=True, cwd=ROOT, env=dict(os.environ, VC_DEBUG="1"), timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "0"
+    assert "interface inBuf:f32,outBuf:f32;N:i32 is blockReduce" in out.stderr
 
 
 def test_load_kernel_from_file(vc, tmp_path):

@@ -298,3 +298,32 @@ def test_poison_fill_outputs(gpu):
     assert "vc: poison vadd output" in before
     assert "vc: poison vadd output" not in inplace      # c shares memory with a
     assert "vc: poison vc.gemm output" in gemm and "256 x 1024 bytes" in gemm
+
+
+def test_glsl_backend_modules_launch(gpu, dev):
+    """Modules shaped like the GLSL backend's (entry "main") resolve by their
+    interface and run the demo kernels: vadd (test/vadd.vc) and blockReduce
+    (test/reduce.vc) with the demos' own launches and exact checks."""
+    from conftest import GLSL_DEMO_INTERFACES, spirv_glsl_module
+    n = 64
+    a = np.arange(n, dtype=np.float32)
+    b = np.full(n, 2.0, np.float32)
+    da, db, dc = dev.put(a), dev.put(b), dev.alloc(4 * n)
+    err, k = gpu.vcLoadKernel(spirv_glsl_module(*GLSL_DEMO_INTERFACES["vadd"]), "main")
+    assert err == gpu.VCError.Success
+    assert gpu.vcLaunchKernel(k, n, 32, [gpu.ptr(da.ptr), gpu.ptr(db.ptr), gpu.ptr(dc.ptr),
+                                         gpu.i32(n)]) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    assert np.array_equal(dc.to_host(np.float32, n), a + b)
+    gpu.vcReleaseKernel(k)
+    N, block = 128, 32
+    x = np.arange(N, dtype=np.float32)
+    dx, dout = dev.put(x), dev.alloc(4 * (N // block))
+    err, k = gpu.vcLoadKernel(spirv_glsl_module(*GLSL_DEMO_INTERFACES["blockReduce"]), "main")
+    assert err == gpu.VCError.Success
+    assert gpu.vcLaunchKernel(k, N, block, [gpu.ptr(dx.ptr), gpu.ptr(dout.ptr), gpu.i32(N)]) == 0
+    assert gpu.vcDeviceSynchronize() == 0
+    expect = x.reshape(-1, block).sum(axis=1)
+    assert np.array_equal(dout.to_host(np.float32, N // block), expect)
+    gpu.vcReleaseKernel(k)
+

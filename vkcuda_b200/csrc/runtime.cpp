@@ -1424,6 +1424,7 @@ const std::vector<KernelEntry> &registry() {
       {"wmma_gemm", k_wmma_gemm, {}},
       {"matmulCoopmat", k_matmul_coopmat, {{"L", 1024}}},
       {"matmulTiled", k_matmul_tiled, {}},
+      {"matmul", k_matmul_tiled, {}},  // test/matmul.vc: the same contract
       {"vc.vadd", k_native_vadd, {}},
       {"vc.sum", k_native_sum, {}},
       {"vc.vadd_sum", k_native_vadd_sum, {}},
@@ -1446,6 +1447,127 @@ VCKernel *make_kernel(const KernelEntry *e) {
   k->entry = e;
   for (auto &c : e->constants) k->constants[c.first] = c.second;
   return k;
+}
+
+// ---- GLSL-backend modules (entry "main"): which demo kernel is this?
+// The VC compiler's GLSL backend gives every pointer parameter its own storage
+// buffer block `layout(set = 0, binding = i) buffer Bi { T name[]; }` in
+// parameter order and gathers the scalar parameters, in order, into one push
+// constant block (lib/Codegen/ASTToGLSL.cpp:955-1008); glslc keeps those
+// member names in the module (OpMemberName). The module's interface, read
+// back here as "name:type,... ; name:type,..." (storage buffers by binding,
+// then push constants), identifies the demo kernel it was compiled from.
+struct SpvInterfaceReader {
+  std::map<uint32_t, std::map<uint32_t, std::string>> member_names;  // struct -> member -> name
+  std::map<uint32_t, std::vector<uint32_t>> struct_members;          // struct -> member type ids
+  std::map<uint32_t, std::string> scalar_types;                      // id -> "f32" / "i32" / ...
+  std::map<uint32_t, uint32_t> runtime_array_elem;                   // id -> element type
+  std::map<uint32_t, std::pair<uint32_t, uint32_t>> pointers;        // id -> (storage class, type)
+  std::map<uint32_t, uint32_t> bindings;                             // variable -> binding
+  std::vector<std::pair<uint32_t, uint32_t>> variables;              // (pointer type, id)
+
+  static std::string literal(const uint32_t *w, size_t n) {
+    std::string out;
+    for (size_t i = 0; i < n; ++i)
+      for (int b = 0; b < 4; ++b) {
+        const char c = static_cast<char>((w[i] >> (8 * b)) & 0xFFu);
+        if (!c) return out;
+        out.push_back(c);
+      }
+    return out;
+  }
+
+  bool read(const uint32_t *words, size_t count) {
+    for (size_t i = 5; i < count;) {
+      const uint32_t op = words[i] & 0xFFFFu, wc = words[i] >> 16;
+      if (wc == 0 || i + wc > count) return false;
+      const uint32_t *a = words + i + 1;
+      const size_t na = wc - 1;
+      switch (op) {
+        case 6:  // OpMemberName
+          if (na >= 3) member_names[a[0]][a[1]] = literal(a + 2, na - 2);
+          break;
+        case 21:  // OpTypeInt
+          if (na >= 3) scalar_types[a[0]] = (a[2] ? "i" : "u") + std::to_string(a[1]);
+          break;
+        case 22:  // OpTypeFloat
+          if (na >= 2) scalar_types[a[0]] = "f" + std::to_string(a[1]);
+          break;
+        case 29:  // OpTypeRuntimeArray
+          if (na >= 2) runtime_array_elem[a[0]] = a[1];
+          break;
+        case 30:  // OpTypeStruct
+          if (na >= 1) struct_members[a[0]].assign(a + 1, a + na);
+          break;
+        case 32:  // OpTypePointer
+          if (na >= 3) pointers[a[0]] = {a[1], a[2]};
+          break;
+        case 59:  // OpVariable
+          if (na >= 3) variables.push_back({a[0], a[1]});
+          break;
+        case 71:  // OpDecorate ... Binding
+          if (na >= 3 && a[1] == 33u) bindings[a[0]] = a[2];
+          break;
+        default:
+          break;
+      }
+      i += wc;
+    }
+    return true;
+  }
+
+  std::string type_name(uint32_t id) const {
+    auto it = scalar_types.find(id);
+    if (it != scalar_types.end()) return it->second;
+    auto ra = runtime_array_elem.find(id);
+    if (ra != runtime_array_elem.end()) return type_name(ra->second);
+    return "?";
+  }
+
+  // "a:f32,b:f32,c:f32;n:i32" (storage buffers by binding; push constants).
+  std::string signature() const {
+    std::map<uint32_t, std::string> buffers;  // binding -> "name:type"
+    std::string push;
+    for (const auto &v : variables) {
+      auto pt = pointers.find(v.first);
+      if (pt == pointers.end()) continue;
+      const uint32_t storage = pt->second.first, st = pt->second.second;
+      auto sm = struct_members.find(st);
+      if (sm == struct_members.end()) continue;
+      auto names = member_names.find(st);
+      auto member = [&](size_t m) {
+        std::string nm = "?";
+        if (names != member_names.end()) {
+          auto it = names->second.find(static_cast<uint32_t>(m));
+          if (it != names->second.end()) nm = it->second;
+        }
+        return nm + ":" + type_name(sm->second[m]);
+      };
+      if (storage == 12u || storage == 2u) {  // StorageBuffer, or Uniform + BufferBlock
+        auto b = bindings.find(v.second);
+        if (b != bindings.end() && sm->second.size() == 1) buffers[b->second] = member(0);
+      } else if (storage == 9u) {  // PushConstant
+        for (size_t m = 0; m < sm->second.size(); ++m) push += (m ? "," : "") + member(m);
+      }
+    }
+    std::string out;
+    for (const auto &b : buffers) out += (out.empty() ? "" : ",") + b.second;
+    return out + ";" + push;
+  }
+};
+
+// Interfaces of the demo kernels as their GLSL modules carry them.
+const char *glsl_kernel_for(const std::string &sig) {
+  static const std::pair<const char *, const char *> table[] = {
+      {"a:f32,b:f32,c:f32;n:i32", "vadd"},                       // test/vadd.vc:12
+      {"inBuf:f32,outBuf:f32;N:i32", "blockReduce"},             // test/reduce.vc:11
+      {"Q:f32,K:f32,V:f32,O:f32;scale:f32,causal:i32", "flashAttn"},  // flash_attn.vc:56
+      {"A:f32,B:f32,C:f32;N:i32", "matmulTiled"},                // matmul_bench.vc:22, test/matmul.vc:12
+      {"a:i32;base:i32,n:i32", "fillPattern"},                   // test/multigpu.vc:24
+  };
+  for (const auto &t : table)
+    if (sig == t.first) return t.second;
+  return nullptr;
 }
 
 uint64_t fnv1a64(const uint32_t *w, size_t n) {
@@ -1488,13 +1610,26 @@ VCError vcLoadKernel(const uint32_t *spirvWords, size_t wordCount, const char *e
   }
   const char *name = entryPoint ? entryPoint : "main";
   const KernelEntry *e = find_entry(name);
-  if (!e) {
-    if (std::strcmp(name, "main") == 0 && spirvWords && wordCount)
+  if (!e && std::strcmp(name, "main") == 0) {
+    // A GLSL-backend module: identify the kernel by its interface.
+    SpvInterfaceReader reader;
+    const std::string sig = reader.read(spirvWords, wordCount) ? reader.signature() : "";
+    const char *kernel = sig.empty() ? nullptr : glsl_kernel_for(sig);
+    if (kernel) {
+      e = find_entry(kernel);
+      const char *dbg = std::getenv("VC_DEBUG");  // loading needs no vcInit
+      if (st().debug || (dbg && std::atoi(dbg) != 0))
+        std::fprintf(stderr, "vc: module 'main' with interface %s is %s\n", sig.c_str(), kernel);
+    } else {
       std::fprintf(stderr,
-                   "vc: entry 'main' names no kernel; module fingerprint %016llx is not registered\n",
-                   (unsigned long long)fnv1a64(spirvWords, wordCount));
-    else
-      std::fprintf(stderr, "vc: no kernel named '%s' in the registry\n", name);
+                   "vc: entry 'main': interface '%s' (module fingerprint %016llx) matches no "
+                   "kernel here\n",
+                   sig.c_str(), (unsigned long long)fnv1a64(spirvWords, wordCount));
+      return VCError::InvalidKernel;
+    }
+  }
+  if (!e) {
+    std::fprintf(stderr, "vc: no kernel named '%s' in the registry\n", name);
     return VCError::InvalidKernel;
   }
   *outKernel = make_kernel(e);
