@@ -117,6 +117,19 @@ def test_glsl_backend_modules_resolve_by_interface(vc):
                                              [("n", "i32")]), "main")[0] == vc.VCError.InvalidKernel
     assert vc.vcLoadKernel(spirv_glsl_module([("a", "f32"), ("b", "f32"), ("c", "f32")], []),
                            "main")[0] == vc.VCError.InvalidKernel
+    # A malformed module (a runtime array whose element type is itself, bound
+    # as an eighth buffer) is refused, not followed.
+    w = spirv_glsl_module(*GLSL_DEMO_INTERFACES["vadd"])
+    w += [(3 << 16) | 29, 900, 900, (3 << 16) | 30, 901, 900,
+          (4 << 16) | 6, 901, 0, int.from_bytes(b"x\0\0\0", "little"),
+          (4 << 16) | 32, 902, 12, 901, (4 << 16) | 59, 902, 903, 12,
+          (4 << 16) | 71, 903, 33, 7]
+    assert vc.vcLoadKernel(w, "main")[0] == vc.VCError.InvalidKernel
+    # Truncated instruction streams end the read, without reading past the end.
+    w = spirv_glsl_module(*GLSL_DEMO_INTERFACES["vadd"])
+    for cut in range(5, len(w), 7):
+        assert vc.vcLoadKernel(w[:cut], "main")[0] in (vc.VCError.InvalidKernel,
+                                                      vc.VCError.Success)
 
 
 def test_glsl_backend_module_identity_is_reported():

@@ -1516,12 +1516,13 @@ struct SpvInterfaceReader {
     return true;
   }
 
+  // A scalar type, or a runtime array of one (one level only: a malformed
+  // module may declare an array of itself).
   std::string type_name(uint32_t id) const {
-    auto it = scalar_types.find(id);
-    if (it != scalar_types.end()) return it->second;
     auto ra = runtime_array_elem.find(id);
-    if (ra != runtime_array_elem.end()) return type_name(ra->second);
-    return "?";
+    if (ra != runtime_array_elem.end()) id = ra->second;
+    auto it = scalar_types.find(id);
+    return it != scalar_types.end() ? it->second : "?";
   }
 
   // "a:f32,b:f32,c:f32;n:i32" (storage buffers by binding; push constants).
