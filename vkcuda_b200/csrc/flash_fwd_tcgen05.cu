@@ -379,13 +379,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
           const float p1 = ex2_approx(x1);
           p[t] = pack2<BF16>(p0, p1);
           // bf16 P (8-bit mantissa): the row sum adds the rounded values so
-          // numerator and denominator use the same weights; fp16 P (11 bits)
-          // is close enough that the unrounded sum keeps O within its bar
-          // and saves the unpacking.
+          // numerator and denominator use the same weights (with one dominant
+          // key the unrounded sum leaves that key's 2^-9 rounding in O: 0.014
+          // against the 1e-2 bar, measured); two mixed-precision adds take
+          // the bf16 halves straight into the fp32 sums. fp16 P (11 bits) is
+          // close enough that the unrounded sum keeps O within its bar.
           const int a = 2 * (t & 1);
           if constexpr (BF16)
-            add2(lsp[a], lsp[a + 1], lsp[a], lsp[a + 1], __uint_as_float(p[t] << 16),
-                 __uint_as_float(p[t] & 0xffff0000u));
+            add_bf16x2_to_f32(lsp[a], lsp[a + 1], p[t]);
           else
             add2(lsp[a], lsp[a + 1], lsp[a], lsp[a + 1], p0, p1);
         }

@@ -582,6 +582,16 @@ __device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, f
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
+// acc_lo += low bf16 of `packed`, acc_hi += high bf16 (each widened exactly,
+// the sum rounded to nearest fp32): sm_100 mixed-precision adds, so packed
+// 16-bit values need no unpacking instructions of their own.
+__device__ __forceinline__ void add_bf16x2_to_f32(float &acc_lo, float &acc_hi, uint32_t packed) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
+      : "+f"(acc_lo), "+f"(acc_hi)
+      : "r"(packed));
+}
+
 // max(a, b, c) in one instruction (three-input max.f32, sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
