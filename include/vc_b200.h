@@ -162,6 +162,12 @@ int vc_kernel_error(int clear);
  * arrives on, bounded to `timeout_us`; returns the error word it set. Used to
  * test the bounded-wait path without hanging a GPU. */
 int vc_selftest_bounded_wait(unsigned timeout_us);
+/* Run the bounds-checked vadd (the form VC_CHECK_BOUNDS=1 selects) over 1024
+ * elements of real memory, telling it the output holds 1000: returns the
+ * error word it set (4, out of bounds, when the check refused indices
+ * 1000..1023 and wrote the rest), 100 when the output is not as expected, -1
+ * on a CUDA error. */
+int vc_selftest_bounds_check(void);
 
 /* ---- 2. native hot-path entries --------------------------------------- */
 

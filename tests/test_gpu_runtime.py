@@ -300,6 +300,62 @@ def test_poison_fill_outputs(gpu):
     assert "vc: poison vc.gemm output" in gemm and "256 x 1024 bytes" in gemm
 
 
+def test_bounds_check_selftest(gpu):
+    """The bounds-checked vadd (what VC_CHECK_BOUNDS=1 selects), told its
+    output holds 1000 of the 1024 elements it is given (all of them real
+    memory), refuses indices 1000..1023 on the device: error word 4, the
+    first 1000 written, the rest untouched; the context stays usable."""
+    assert gpu.selftest_bounds_check() == 4
+    assert gpu.kernel_error(True) == 0
+
+
+def test_check_bounds_env_runs_checked_forms(gpu):
+    """VC_CHECK_BOUNDS=1: vadd, fillPattern and blockReduce (registry launches)
+    and the native vadd / block-reduce entries run their bounds-checked forms
+    with in-range launches: exact results, a clean error word, and each launch
+    named in the VC_DEBUG log."""
+    r = _child("from vkcuda_b200 import vc\n"
+               "import numpy as np\n"
+               "assert vc.vcInit() == 0\n"
+               "n = 1000\n"
+               "a = np.arange(n, dtype=np.float32); b = np.full(n, 2.0, np.float32)\n"
+               "e, da = vc.vcMalloc(4 * n); e, db = vc.vcMalloc(4 * n); e, dc = vc.vcMalloc(4 * n)\n"
+               "assert vc.vcMemcpy(da, a, 4 * n, vc.VCMemcpyKind.HostToDevice) == 0\n"
+               "assert vc.vcMemcpy(db, b, 4 * n, vc.VCMemcpyKind.HostToDevice) == 0\n"
+               "e, k = vc.vcGetKernel('vadd')\n"
+               "assert vc.vcLaunchKernel(k, n, 32, [vc.ptr(da), vc.ptr(db), vc.ptr(dc), vc.i32(n)]) == 0\n"
+               "c = np.empty(n, np.float32)\n"
+               "assert vc.vcMemcpy(c, dc, 4 * n, vc.VCMemcpyKind.DeviceToHost) == 0\n"
+               "assert np.array_equal(c, a + b)\n"
+               "assert vc.vadd_f32(da, db, dc, n) == 0 and vc.vcDeviceSynchronize() == 0\n"
+               "assert vc.vcMemcpy(c, dc, 4 * n, vc.VCMemcpyKind.DeviceToHost) == 0\n"
+               "assert np.array_equal(c, a + b)\n"
+               "e, k = vc.vcGetKernel('fillPattern')\n"
+               "assert vc.vcLaunchKernel(k, n, 32, [vc.ptr(dc), vc.i32(7), vc.i32(n)]) == 0\n"
+               "ci = np.empty(n, np.int32)\n"
+               "assert vc.vcMemcpy(ci, dc, 4 * n, vc.VCMemcpyKind.DeviceToHost) == 0\n"
+               "assert np.array_equal(ci, 7 + np.arange(n, dtype=np.int32))\n"
+               "e, k = vc.vcGetKernel('blockReduce')\n"
+               "N, block = 1024, 32\n"
+               "x = np.arange(N, dtype=np.float32)\n"
+               "e, dx = vc.vcMalloc(4 * N); e, do = vc.vcMalloc(4 * (N // block))\n"
+               "assert vc.vcMemcpy(dx, x, 4 * N, vc.VCMemcpyKind.HostToDevice) == 0\n"
+               "assert vc.vcLaunchKernel(k, N, block, [vc.ptr(dx), vc.ptr(do), vc.i32(N)]) == 0\n"
+               "out = np.empty(N // block, np.float32)\n"
+               "assert vc.vcMemcpy(out, do, out.nbytes, vc.VCMemcpyKind.DeviceToHost) == 0\n"
+               "assert np.array_equal(out, x.reshape(-1, block).sum(axis=1))\n"
+               "assert vc.block_reduce_f32(dx, do, N, block, N // block) == 0\n"
+               "assert vc.vcDeviceSynchronize() == 0\n"
+               "assert vc.vcMemcpy(out, do, out.nbytes, vc.VCMemcpyKind.DeviceToHost) == 0\n"
+               "assert np.array_equal(out, x.reshape(-1, block).sum(axis=1))\n"
+               "assert vc.kernel_error(True) == 0\n"
+               "assert vc.vcShutdown() == 0\n",
+               {"VC_CHECK_BOUNDS": "1", "VC_DEBUG": "1"})
+    assert r.returncode == 0, r.stderr
+    for name in ("vadd", "vc_vadd_f32", "fillPattern", "blockReduce", "vc_block_reduce_f32"):
+        assert f"vc: bounds-checked {name} launch" in r.stderr, name
+
+
 def test_glsl_backend_modules_launch(gpu, dev):
     """Modules shaped like the GLSL backend's (entry "main") resolve by their
     interface and run the demo kernels: vadd (test/vadd.vc) and blockReduce

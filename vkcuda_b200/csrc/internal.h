@@ -51,8 +51,18 @@ cudaError_t launch_sum_f32_noalloc(const float *x, int64_t n, double *out, cudaS
                                    int *blocks_needed);
 // a[i] = base + i for i < n (the multi-device demo's pattern fill).
 cudaError_t launch_fill_pattern(int *a, int base, int64_t n, cudaStream_t stream);
+// Block reduce with the reference's pairing; lim_in >= 0 selects the
+// bounds-checked form (lim_in / lim_out: elements in and out hold).
 cudaError_t launch_block_reduce_demo(const float *in, float *out, int n, int block,
-                                     int groups, cudaStream_t stream);
+                                     int groups, cudaStream_t stream, int64_t lim_in = -1,
+                                     int64_t lim_out = -1);
+// Bounds-checked forms (VC_CHECK_BOUNDS=1): each access is checked against
+// the elements its buffer holds; a miss records kErrOutOfBounds and is skipped.
+cudaError_t launch_fill_pattern_checked(int *a, int base, int64_t n, int64_t lim,
+                                        cudaStream_t stream);
+cudaError_t launch_vadd_f32_checked(const float *a, const float *b, float *c, int64_t n,
+                                    int64_t lim_a, int64_t lim_b, int64_t lim_c,
+                                    cudaStream_t stream);
 
 // ---- GEMM (gemm_tcgen05.cu, gemm_simt.cu)
 struct GemmArgs {

@@ -23,6 +23,7 @@ enum DeviceErrorCode : unsigned int {
   kErrWaitTimeout = 1,   // an mbarrier wait passed its deadline
   kErrBadShape = 2,      // kernel saw a launch shape it cannot serve
   kErrSelfTest = 3,      // the bounded-wait self test timed out (expected)
+  kErrOutOfBounds = 4,   // a bounds-checked kernel met an index past its buffer
 };
 
 __device__ __forceinline__ void record_error(unsigned int code) {

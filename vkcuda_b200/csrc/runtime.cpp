@@ -116,6 +116,7 @@ struct State {
   bool profile = false;
   bool debug = false;
   bool poison = false;  // VC_POISON=1: NaN canaries in outputs before launches
+  bool check_bounds = false;  // VC_CHECK_BOUNDS=1: device-side index checks
   long sync_timeout_ms = 0;
   std::map<uintptr_t, AllocInfo> allocs;
   std::unordered_map<void *, int> stream_device;
@@ -387,6 +388,8 @@ VCError vcInit() {
   S.profile = std::getenv("VC_PROFILE") && std::atoi(std::getenv("VC_PROFILE")) != 0;
   S.debug = std::getenv("VC_DEBUG") && std::atoi(std::getenv("VC_DEBUG")) != 0;
   S.poison = std::getenv("VC_POISON") && std::atoi(std::getenv("VC_POISON")) != 0;
+  S.check_bounds =
+      std::getenv("VC_CHECK_BOUNDS") && std::atoi(std::getenv("VC_CHECK_BOUNDS")) != 0;
   S.sync_timeout_ms = std::getenv("VC_SYNC_TIMEOUT_MS") ? std::atol(std::getenv("VC_SYNC_TIMEOUT_MS")) : 0;
   parse_faults_locked(S);
   S.initialized = true;
@@ -1118,6 +1121,38 @@ void poison_output(const char *kernel, void *p, size_t bytes, cudaStream_t s,
   poison_output(kernel, p, bytes, bytes, 1, s, inputs);
 }
 
+// ---- VC_CHECK_BOUNDS=1: the demo kernels (vadd, fillPattern, blockReduce
+// and their native entries) run their bounds-checked forms, in which every
+// global access is checked on the device against the extent the allocation
+// registry records for its buffer; an index past it sets kErrOutOfBounds in
+// the error word (vc_kernel_error) and is skipped. The host checks above each
+// launch use the same extents, so a check that fires means the kernel's own
+// index arithmetic went wrong. (The TMA kernels need no such form: their
+// tensor maps bound every copy in hardware.)
+int64_t elems_available(const void *p, size_t esz) {
+  const size_t b = bytes_available(p);
+  return b == SIZE_MAX ? INT64_MAX : (int64_t)(b / esz);
+}
+bool checking(const char *name) {
+  if (!st().check_bounds) return false;
+  if (st().debug) std::fprintf(stderr, "vc: bounds-checked %s launch\n", name);
+  return true;
+}
+cudaError_t vadd_maybe_checked(const float *a, const float *b, float *c, int64_t n,
+                               cudaStream_t s, const char *name) {
+  if (checking(name))
+    return vcb::launch_vadd_f32_checked(a, b, c, n, elems_available(a, 4), elems_available(b, 4),
+                                        elems_available(c, 4), s);
+  return vcb::launch_vadd_f32(a, b, c, n, s);
+}
+cudaError_t block_reduce_maybe_checked(const float *in, float *out, int n, int block, int groups,
+                                       cudaStream_t s, const char *name) {
+  if (checking(name))
+    return vcb::launch_block_reduce_demo(in, out, n, block, groups, s, elems_available(in, 4),
+                                         elems_available(out, 4));
+  return vcb::launch_block_reduce_demo(in, out, n, block, groups, s);
+}
+
 // vadd(a, b, c, int n): c[i] = a[i] + b[i] for i < min(n, workgroups*block)
 // (test/vadd.vc:12-17).
 VCError k_vadd(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, int n, cudaStream_t s) {
@@ -1133,7 +1168,8 @@ VCError k_vadd(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, int n, c
   if (bytes > bytes_available(pa) || bytes > bytes_available(pb) || bytes > bytes_available(pc))
     return too_small("vadd");
   poison_output("vadd", const_cast<void *>(pc), bytes, s, {{pa, bytes}, {pb, bytes}});
-  return run(vcb::launch_vadd_f32((const float *)pa, (const float *)pb, (float *)pc, m, s), "vadd");
+  return run(vadd_maybe_checked((const float *)pa, (const float *)pb, (float *)pc, m, s, "vadd"),
+             "vadd");
 }
 
 // fillPattern(int *a, int base, int n): a[i] = base + i for
@@ -1149,6 +1185,9 @@ VCError k_fill_pattern(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, 
   if (m <= 0) return VCError::Success;
   if ((size_t)m * 4 > bytes_available(pa)) return too_small("fillPattern");
   poison_output("fillPattern", const_cast<void *>(pa), (size_t)m * 4, s, {});
+  if (checking("fillPattern"))
+    return run(vcb::launch_fill_pattern_checked((int *)pa, (int)base, m, elems_available(pa, 4), s),
+               "fillPattern");
   return run(vcb::launch_fill_pattern((int *)pa, (int)base, m, s), "fillPattern");
 }
 
@@ -1166,8 +1205,9 @@ VCError k_block_reduce(VCKernel &, const LaunchShape &sh, const VCKernelArg *a, 
   if (need > 0 && (size_t)need * 4 > bytes_available(pin)) return too_small("blockReduce");
   poison_output("blockReduce", const_cast<void *>(pout), (size_t)groups * 4, s,
                 {{pin, need > 0 ? (size_t)need * 4 : 0}});
-  return run(vcb::launch_block_reduce_demo((const float *)pin, (float *)pout, (int)N, (int)sh.bx,
-                                           (int)groups, s), "blockReduce");
+  return run(block_reduce_maybe_checked((const float *)pin, (float *)pout, (int)N, (int)sh.bx,
+                                        (int)groups, s, "blockReduce"),
+             "blockReduce");
 }
 
 // flashAttn(Q, K, V, O, float scale, int causal) with the demo's compile-time
@@ -1299,7 +1339,8 @@ VCError k_native_vadd(VCKernel &, const LaunchShape &, const VCKernelArg *a, int
   if (bytes > bytes_available(pa) || bytes > bytes_available(pb) || bytes > bytes_available(pc))
     return too_small("vc.vadd");
   poison_output("vc.vadd", const_cast<void *>(pc), bytes, s, {{pa, bytes}, {pb, bytes}});
-  return run(vcb::launch_vadd_f32((const float *)pa, (const float *)pb, (float *)pc, cnt, s), "vc.vadd");
+  return run(vadd_maybe_checked((const float *)pa, (const float *)pb, (float *)pc, cnt, s, "vc.vadd"),
+             "vc.vadd");
 }
 
 VCError sum_common(const float *x, const float *b, float *c, long long cnt, double *out,
@@ -1351,8 +1392,9 @@ VCError k_native_block_reduce(VCKernel &, const LaunchShape &, const VCKernelArg
   if ((size_t)groups * 4 > bytes_available(pout)) return too_small("vc.block_reduce");
   poison_output("vc.block_reduce", const_cast<void *>(pout), (size_t)groups * 4, s,
                 {{pin, N > 0 ? (size_t)N * 4 : 0}});
-  return run(vcb::launch_block_reduce_demo((const float *)pin, (float *)pout, (int)N, (int)block,
-                                           (int)groups, s), "vc.block_reduce");
+  return run(block_reduce_maybe_checked((const float *)pin, (float *)pout, (int)N, (int)block,
+                                        (int)groups, s, "vc.block_reduce"),
+             "vc.block_reduce");
 }
 
 VCError gemm_checked(const vcb::GemmArgs &g, int dtype, cudaStream_t s) {
@@ -1914,6 +1956,36 @@ int vc_kernel_error(int clear) {
     if (c != 0) return c;
   return 0;
 }
+int vc_selftest_bounds_check(void) {
+  if (!ensure_init()) return -1;
+  use_current_device();
+  // 1024 elements each, all of them real memory; the checked vadd is told c
+  // holds 1000, so indices 1000..1023 must be refused on the device.
+  constexpr int64_t kN = 1024, kLimit = 1000;
+  float *buf = nullptr;
+  if (cudaMalloc(&buf, 3 * kN * sizeof(float)) != cudaSuccess) return -1;
+  float *a = buf, *b = buf + kN, *c = buf + 2 * kN;
+  int rc = -1;
+  std::vector<float> ha(kN), hc(kN);
+  for (int64_t i = 0; i < kN; ++i) ha[i] = (float)i;
+  vcb::stream_kernels_error(1);
+  if (cudaMemcpy(a, ha.data(), kN * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+      cudaMemcpy(b, ha.data(), kN * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+      cudaMemset(c, 0xFF, kN * 4) == cudaSuccess &&
+      vcb::launch_vadd_f32_checked(a, b, c, kN, kN, kN, kLimit, nullptr) == cudaSuccess &&
+      cudaDeviceSynchronize() == cudaSuccess &&
+      cudaMemcpy(hc.data(), c, kN * 4, cudaMemcpyDeviceToHost) == cudaSuccess) {
+    rc = vcb::stream_kernels_error(1);  // expected: kErrOutOfBounds (4)
+    for (int64_t i = 0; i < kN && rc == 4; ++i) {
+      uint32_t bits;
+      std::memcpy(&bits, &hc[i], 4);
+      const bool want_written = i < kLimit;
+      if (want_written ? hc[i] != 2.0f * (float)i : bits != 0xFFFFFFFFu) rc = 100;
+    }
+  }
+  cudaFree(buf);
+  return rc;
+}
 int vc_selftest_bounded_wait(unsigned timeout_us) {
   if (!ensure_init()) return -1;
   use_current_device();
@@ -1930,7 +2002,8 @@ int vc_vadd_f32(const float *a, const float *b, float *c, int64_t n, void *s) {
   use_current_device();
   const size_t bytes = (size_t)n * 4;
   poison_output("vc_vadd_f32", c, bytes, reinterpret_cast<cudaStream_t>(s), {{a, bytes}, {b, bytes}});
-  return E(map_cuda(vcb::launch_vadd_f32(a, b, c, n, reinterpret_cast<cudaStream_t>(s)), "vc_vadd_f32"));
+  return E(map_cuda(vadd_maybe_checked(a, b, c, n, reinterpret_cast<cudaStream_t>(s), "vc_vadd_f32"),
+                    "vc_vadd_f32"));
 }
 int vc_sum_f32(const float *x, int64_t n, double *out, void *s) {
   if (!x || !out || n < 0) return E(VCError::InvalidValue);
@@ -2035,8 +2108,9 @@ int vc_block_reduce_f32(const float *in, float *out, int n, int block, int group
   use_current_device();
   poison_output("vc_block_reduce_f32", out, (size_t)groups * 4, reinterpret_cast<cudaStream_t>(s),
                 {{in, (size_t)n * 4}});
-  return E(map_cuda(vcb::launch_block_reduce_demo(in, out, n, block, groups,
-                                                  reinterpret_cast<cudaStream_t>(s)),
+  return E(map_cuda(block_reduce_maybe_checked(in, out, n, block, groups,
+                                               reinterpret_cast<cudaStream_t>(s),
+                                               "vc_block_reduce_f32"),
                     "vc_block_reduce_f32"));
 }
 int vc_gemm(const void *A, const void *B, float *D, const float *Cin, int M, int N, int K,

@@ -230,13 +230,30 @@ sum_scalar_kernel(const float *__restrict__ x, const float *__restrict__ b,
 // slots (lane t reads lane t + s, and slots >= s are never written at that
 // level), so each partial is bit-identical to the reference for any block
 // size, power of two or not.
+//
+// VC_CHECK_BOUNDS=1 forms of the demo kernels (debug aid): the same loops
+// with every global access checked against the elements its buffer holds
+// from the pointer on (the allocation registry's figure; INT64_MAX for memory
+// the registry does not know). An index past its limit records
+// kErrOutOfBounds in the error word and the access is skipped, so a wrong
+// index ends the launch with a status the host reads instead of a fault.
+struct AccessLimits {
+  int64_t a, b, c;  // elements readable / writable from each pointer
+};
+__device__ __forceinline__ bool in_limit(int64_t i, int64_t limit) {
+  if (i < limit) return true;
+  record_error(kErrOutOfBounds);
+  return false;
+}
+
+template <bool CHECK>
 __global__ void block_reduce_demo_kernel(const float *__restrict__ in,
                                          float *__restrict__ out, int n,
-                                         int block) {
+                                         int block, AccessLimits lim) {
   extern __shared__ float slots[];
   const int t = threadIdx.x;
   const int64_t i = static_cast<int64_t>(blockIdx.x) * block + t;
-  slots[t] = (t < block && i < n) ? in[i] : 0.0f;
+  slots[t] = (t < block && i < n && (!CHECK || in_limit(i, lim.a))) ? in[i] : 0.0f;
   __syncthreads();
   int s = block / 2;
   // Shared-memory levels until every slot that can still contribute
@@ -253,7 +270,7 @@ __global__ void block_reduce_demo_kernel(const float *__restrict__ in,
       const float other = __shfl_down_sync(0xffffffffu, v, s);
       if (t < s) v = v + other;
     }
-    if (t == 0) out[blockIdx.x] = v;
+    if (t == 0 && (!CHECK || in_limit(blockIdx.x, lim.c))) out[blockIdx.x] = v;
   }
 }
 
@@ -261,11 +278,21 @@ __global__ void fill_f64_kernel(double *p, double v) { *p = v; }
 
 // a[i] = base + i for i < n (test/multigpu.vc:24-27, the multi-device demo's
 // pattern fill), grid-stride.
-__global__ void fill_pattern_kernel(int *__restrict__ a, int base, int64_t n) {
+template <bool CHECK>
+__global__ void fill_pattern_kernel(int *__restrict__ a, int base, int64_t n, int64_t lim) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += stride)
-    a[i] = base + static_cast<int>(i);
+    if (!CHECK || in_limit(i, lim)) a[i] = base + static_cast<int>(i);
+}
+
+// Bounds-checked vadd (scalar: a debug path, not a fast one).
+__global__ void vadd_checked_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                                    float *__restrict__ c, int64_t n, AccessLimits lim) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride)
+    if (in_limit(i, lim.a) && in_limit(i, lim.b) && in_limit(i, lim.c)) c[i] = a[i] + b[i];
 }
 
 int resident_per_sm();
@@ -394,17 +421,40 @@ cudaError_t launch_sum_f32(const float *x, const float *b, float *c, int64_t n,
 
 cudaError_t launch_fill_pattern(int *a, int base, int64_t n, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
-  fill_pattern_kernel<<<stream_grid(n / kUnroll + 1), kStreamThreads, 0, stream>>>(a, base, n);
+  fill_pattern_kernel<false><<<stream_grid(n / kUnroll + 1), kStreamThreads, 0, stream>>>(
+      a, base, n, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill_pattern_checked(int *a, int base, int64_t n, int64_t lim,
+                                        cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  fill_pattern_kernel<true><<<stream_grid(n / kUnroll + 1), kStreamThreads, 0, stream>>>(
+      a, base, n, lim);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_vadd_f32_checked(const float *a, const float *b, float *c, int64_t n,
+                                    int64_t lim_a, int64_t lim_b, int64_t lim_c,
+                                    cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  vadd_checked_kernel<<<stream_grid(n / kUnroll + 1), kStreamThreads, 0, stream>>>(
+      a, b, c, n, AccessLimits{lim_a, lim_b, lim_c});
   return cudaGetLastError();
 }
 
 cudaError_t launch_block_reduce_demo(const float *in, float *out, int n, int block,
-                                     int groups, cudaStream_t stream) {
+                                     int groups, cudaStream_t stream, int64_t lim_in,
+                                     int64_t lim_out) {
   if (block <= 0 || block > 1024 || groups <= 0) return cudaErrorInvalidValue;
   // Threads: at least one warp so the shuffle levels have 32 lanes.
   const int threads = block < 32 ? 32 : ((block + 31) / 32) * 32;
-  block_reduce_demo_kernel<<<groups, threads, threads * sizeof(float), stream>>>(
-      in, out, n, block);
+  if (lim_in < 0)
+    block_reduce_demo_kernel<false><<<groups, threads, threads * sizeof(float), stream>>>(
+        in, out, n, block, AccessLimits{0, 0, 0});
+  else
+    block_reduce_demo_kernel<true><<<groups, threads, threads * sizeof(float), stream>>>(
+        in, out, n, block, AccessLimits{lim_in, 0, lim_out});
   return cudaGetLastError();
 }
 

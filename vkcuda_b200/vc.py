@@ -138,6 +138,7 @@ SIGNATURES = {
     "vc_get_kernel": (_I, [ctypes.c_char_p, _PVP]),
     "vc_kernel_set_constant": (_I, [_VP, ctypes.c_char_p, _LL]),
     "vc_kernel_error": (_I, [_I]), "vc_selftest_bounded_wait": (_I, [_U]),
+    "vc_selftest_bounds_check": (_I, []),
     "vc_vadd_f32": (_I, [_VP, _VP, _VP, _I64, _VP]),
     "vc_sum_f32": (_I, [_VP, _I64, _VP, _VP]),
     "vc_sum_f32_noalloc": (_I, [_VP, _I64, _VP, _VP]),
@@ -476,6 +477,12 @@ def kernel_error(clear: bool = True) -> int:
 
 def selftest_bounded_wait(timeout_us: int) -> int:
     return library().vc_selftest_bounded_wait(timeout_us)
+
+
+def selftest_bounds_check() -> int:
+    """Bounds-checked vadd told its output holds 1000 of 1024 elements:
+    4 (kErrOutOfBounds) when the device check refused the rest."""
+    return library().vc_selftest_bounds_check()
 
 
 # ------------------------------------------------------------ native entries
