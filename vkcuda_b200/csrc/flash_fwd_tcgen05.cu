@@ -49,13 +49,22 @@
 // Probes put the loss in contention with the rest of the SM: busy warps on
 // the issuer's sub-partition (72 cycles per MMA with FMA-bound neighbours),
 // softmax TMEM loads (75 with continuous loads), the K/V TMA writes (~5 %:
-// the same kernel without refills). Handing P over in two halves, so the
-// first half's PV MMAs run under the second half's exponentials, gave +3.6 %
-// (causal N=4096) to +9 % (N=8192); tried and slower: exponentials partly on
-// an FMA-pipe polynomial (-1 .. -5 %), P in four parts (-3 .. -4 % against
-// halves), one issuing thread per query tile (-15 %: the two tiles' MMAs
-// interleave in the tensor queue and each tile's S finishes later), K and V
-// of a key tile on one barrier (-0.5 %), a persistent grid (-1 .. -5 %).
+// the same kernel without refills). Per tile, S done -> softmax -> hand-offs
+// -> that tile's remaining MMAs -> next S done is a dependency loop as long
+// as the step, while the issuer is busy for the same time: both sides are
+// critical. Handing P over in two halves, so the first half's PV MMAs run
+// under the second half's exponentials, gave +3.6 % (causal N=4096) to +9 %
+// (N=8192). Tried and slower (A/B on one box): part of the exponentials on
+// the FMA pipe (a cubic 2^x, floor by an add rounded down; MUFU, at 16
+// exponentials per clock per SM, is not the binding unit: -1 .. -9 % with
+// the share), P in four parts (-3 .. -4 % against halves), one issuing
+// thread per query tile (-15 %: the two tiles' MMAs interleave in the tensor
+// queue and each tile's S finishes later), barrier tests issued a few MMAs
+// ahead (-0.6 .. -2.4 %), the whole warp issuing with elect.sync (-0.2 ..
+// -3.6 %), the first half of P against the running max with the row max
+// alongside (-9 %), CTA pairs with cta_group::2 MMAs (-31 .. -34 %: the
+// cross-CTA hand-offs lengthen the loop), K and V of a key tile on one
+// barrier (-0.5 %), a persistent grid (-1 .. -5 %).
 // Roofline: 4*BH*N^2*d FLOP (2*BH*N^2*d causal) against the dense tensor peak.
 #include <cuda.h>
 #include <cuda_bf16.h>
