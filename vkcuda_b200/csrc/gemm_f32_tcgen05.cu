@@ -280,6 +280,25 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (CTA 0)
+      // Descriptors (raw and packed A / B of stage 0) built once and advanced
+      // by 32-bit adds to their address field (addresses below 256 KiB: no
+      // carry): fewer instructions per MMA on the issuing thread.
+      const uint32_t a_raw0 = smem_u32(stage_base);
+      const uint32_t b_raw0 = a_raw0 + kTileBytes;
+      const uint64_t d_ar = smem_desc_sw128(a_raw0, 16, 1024);
+      const uint64_t d_br = b_kn ? smem_desc_sw128_atom32(b_raw0, BK * 128, 512)
+                                 : smem_desc_sw128(b_raw0, 16, 1024);
+      const uint64_t d_ap = smem_desc_sw128(a_raw0 + kRawBytes, 16, 1024);
+      const uint64_t d_bp = b_kn ? smem_desc_sw128(b_raw0 + kRawBytes, 64 * 128, 1024)
+                                 : smem_desc_sw128(b_raw0 + kRawBytes, 16, 1024);
+      const uint32_t ar_lo = (uint32_t)d_ar, ar_hi = (uint32_t)(d_ar >> 32);
+      const uint32_t br_lo = (uint32_t)d_br, br_hi = (uint32_t)(d_br >> 32);
+      const uint32_t ap_lo = (uint32_t)d_ap, ap_hi = (uint32_t)(d_ap >> 32);
+      const uint32_t bp_lo = (uint32_t)d_bp, bp_hi = (uint32_t)(d_bp >> 32);
+      // Per 8-deep step g (descriptor address units of 16 bytes).
+      const uint32_t br_step = b_kn ? 1024 >> 4 : 32 >> 4;
+      const uint32_t bp_step = b_kn ? 2048 >> 4 : 32 >> 4;
+      const uint32_t empty_lead = lead(&bars->empty[0]), empty_peer = peer(&bars->empty[0]);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -302,31 +321,25 @@ gemm_f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
           // the tensor proxy before its release arrive) precede these MMAs.
           if (!mbar_wait_cluster(&bars->split[stage], phase)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_raw = smem_u32(stage_base + stage * kStageBytes);
-          const uint32_t b_raw = a_raw + kTileBytes;
-          const uint32_t a_pk = a_raw + kRawBytes;
-          const uint32_t b_pk = b_raw + kRawBytes;
+          const uint32_t soff = (stage * kStageBytes) >> 4;
 #pragma unroll
           for (int g = 0; g < BK / 8; ++g) {
             // hi*hi: tf32 from the raw tiles. K-major: 8 fp32 = 32 bytes per
             // step inside the swizzle row. MN-major B (32-byte-atom
             // swizzle): 8 K-rows = 1024 bytes per step, 4-row groups 512
             // bytes apart, 32-column blocks BK x 128 bytes apart.
-            const uint64_t ad = smem_desc_sw128(a_raw + g * 32, 16, 1024);
-            const uint64_t bd = b_kn ? smem_desc_sw128_atom32(b_raw + g * 1024, BK * 128, 512)
-                                     : smem_desc_sw128(b_raw + g * 32, 16, 1024);
+            mma_tf32_ss_pair_lohi(d_tmem, ar_lo + soff + g * (32 >> 4), ar_hi,
+                                  br_lo + soff + g * br_step, br_hi, idesc,
+                                  (kb != kb0 || g != 0) ? 1u : 0u);
             // lo*hi + hi*lo: one bf16 MMA of K = 16 over the packed tiles.
             // K-major: 16 bf16 = 32 bytes per step. MN-major B: 16 K-rows =
             // 2048 bytes per step, 8-row groups 1024 apart, 64-column blocks
             // 64 x 128 bytes apart.
-            const uint64_t apd = smem_desc_sw128(a_pk + g * 32, 16, 1024);
-            const uint64_t bpd = b_kn ? smem_desc_sw128(b_pk + g * 2048, 64 * 128, 1024)
-                                      : smem_desc_sw128(b_pk + g * 32, 16, 1024);
-            mma_tf32_ss_pair(d_tmem, ad, bd, idesc, (kb != kb0 || g != 0) ? 1u : 0u);
-            mma_f16_ss_pair(d_tmem, apd, bpd, idesc16, 1u);
+            mma_f16_ss_pair_lohi(d_tmem, ap_lo + soff + g * (32 >> 4), ap_hi,
+                                 bp_lo + soff + g * bp_step, bp_hi, idesc16, 1u);
           }
-          mma_commit_pair(lead(&bars->empty[stage]));
-          mma_commit_pair(peer(&bars->empty[stage]));
+          mma_commit_pair(empty_lead + stage * 8);
+          mma_commit_pair(empty_peer + stage * 8);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;

@@ -198,6 +198,15 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
+      // Descriptors built once, advanced by 32-bit adds to their address
+      // field (every address here is below 256 KiB: no carry out of it).
+      const uint32_t base_addr = smem_u32(stage_base);
+      const uint64_t da0 = smem_desc_sw128(base_addr, 16, 1024);
+      const uint64_t db0 = b_kn ? smem_desc_sw128(base_addr + kABytes, 64 * BK * 2, 1024)
+                                : smem_desc_sw128(base_addr + kABytes, 16, 1024);
+      const uint32_t da_lo = (uint32_t)da0, da_hi = (uint32_t)(da0 >> 32);
+      const uint32_t db_lo = (uint32_t)db0, db_hi = (uint32_t)(db0 >> 32);
+      const uint32_t b_kstep = b_kn ? (16 * 128) >> 4 : 32 >> 4;  // per K = 16
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -212,16 +221,11 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&bars->full[stage], phase)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(stage_base + stage * kStageBytes);
-          const uint32_t b_addr = a_addr + kABytes;
+          const uint32_t soff = (stage * kStageBytes) >> 4;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bdesc =
-                b_kn ? smem_desc_sw128(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
-                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_ss_lohi(d_tmem, da_lo + soff + k * (32 >> 4), da_hi, db_lo + soff + k * b_kstep,
+                            db_hi, idesc, (kb | k) != 0 ? 1u : 0u);
           mma_commit(&bars->empty[stage]);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
@@ -430,6 +434,19 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (CTA 0)
+      // Descriptors and the two CTAs' barrier addresses built once and
+      // advanced by 32-bit adds: each instruction this thread issues per MMA
+      // delays the MMAs (with descriptors rebuilt per MMA the issue pace,
+      // not the tensor pipe, set the mainloop's rate: tail half-units, half
+      // the MMA work, took as long as full units).
+      const uint32_t base_addr = smem_u32(stage_base);
+      const uint64_t da0 = smem_desc_sw128(base_addr, 16, 1024);
+      const uint64_t db0 = b_kn ? smem_desc_sw128(base_addr + kPairABytes, 64 * BK * 2, 1024)
+                                : smem_desc_sw128(base_addr + kPairABytes, 16, 1024);
+      const uint32_t da_lo = (uint32_t)da0, da_hi = (uint32_t)(da0 >> 32);
+      const uint32_t db_lo = (uint32_t)db0, db_hi = (uint32_t)(db0 >> 32);
+      const uint32_t b_kstep = b_kn ? (16 * 128) >> 4 : 32 >> 4;  // per K = 16
+      const uint32_t empty_lead = lead(&bars->empty[0]), empty_peer = peer(&bars->empty[0]);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -444,18 +461,14 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&bars->full[stage], phase)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(stage_base + stage * kPairStageBytes);
-          const uint32_t b_addr = a_addr + kPairABytes;
+          const uint32_t soff = (stage * kPairStageBytes) >> 4;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bdesc =
-                b_kn ? smem_desc_sw128(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
-                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
-          }
-          mma_commit_pair(lead(&bars->empty[stage]));
-          mma_commit_pair(peer(&bars->empty[stage]));
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_ss_pair_lohi(d_tmem, da_lo + soff + k * (32 >> 4), da_hi,
+                                 db_lo + soff + k * b_kstep, db_hi, idesc,
+                                 (kb | k) != 0 ? 1u : 0u);
+          mma_commit_pair(empty_lead + stage * 8);
+          mma_commit_pair(empty_peer + stage * 8);
           if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
