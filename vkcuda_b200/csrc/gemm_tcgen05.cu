@@ -290,7 +290,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
 // its 128 accumulator rows (2 x 256 columns, double-buffered). Work units are
 // 256 x 256 pair tiles; a tail wave that fills at most half the clusters is
 // split into 256 x 128 halves.
-constexpr int kPairStages = 6;
+constexpr int kPairStages = 3;  // of kPairSub K blocks each
 // Tile-order groups of 8 pair rows when the B operand exceeds this many bytes
 // (it then no longer stays in L2 with row-major order: 8192^3 +6 %, while
 // 4096^3, whose B fits, measured 1.5 % faster row-major).
@@ -298,7 +298,13 @@ constexpr int kGroupRows = 8;
 constexpr size_t kGroupAboveBBytes = 64ull << 20;
 constexpr uint32_t kPairABytes = 128 * BK * 2;  // this CTA's A rows
 constexpr uint32_t kPairBBytes = 128 * BK * 2;  // this CTA's half of the B panel
-constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;
+constexpr uint32_t kPairSubBytes = kPairABytes + kPairBBytes;  // one 64-deep K block
+// Each barrier stage holds kPairSub consecutive 64-deep K blocks: per stage
+// the issuing thread waits once and commits once per CTA for 8 MMAs instead
+// of 4 (it was the bottleneck: ~580 cycles of issue per 64-deep block against
+// 512 of MMA, measured).
+constexpr int kPairSub = 2;
+constexpr uint32_t kPairStageBytes = kPairSub * kPairSubBytes;
 
 struct __align__(8) PairBarriers {
   uint64_t full[kPairStages];   // used in CTA 0
@@ -333,7 +339,7 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   const int num_clusters = gridDim.x >> 1;
   const int tiles_n = (N + BN - 1) / BN;
   const int tiles_m = (M + 2 * BM - 1) / (2 * BM);
-  const int kblocks = (K + BK - 1) / BK;
+  const int kstages = ((K + BK - 1) / BK + kPairSub - 1) / kPairSub;  // barrier stages per unit
   // Tile order: groups of `group_rows` pair rows, column by column within a
   // group, so the tiles in flight (one per cluster) share a few A and B
   // panels that stay in L2 even when all of B does not (8192^3, groups of 8:
@@ -404,19 +410,25 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         // (loading the full 128 made the tail's half units as slow as full
         // tiles: the stage copies, not the MMAs, set their pace).
         const bool half = width < BN;
-        const uint32_t stage_bytes = kPairABytes + (half ? kPairBBytes / 2 : kPairBBytes);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const uint32_t sub_bytes = kPairABytes + (half ? kPairBBytes / 2 : kPairBBytes);
+        // A K block past K (odd block count) loads as zeros (TMA fill) and
+        // adds nothing.
+        for (int ks = 0; ks < kstages; ++ks) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1u)) { ok = false; break; }
-          uint8_t *sA = stage_base + stage * kPairStageBytes;
-          uint8_t *sB = sA + kPairABytes;
-          if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * stage_bytes);
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * kPairSub * sub_bytes);
           const uint32_t fb = lead(&bars->full[stage]);
-          tma_load_2d_pair(sA, &tmA, kb * BK, a_row, fb);
-          if (b_kn) {
-            tma_load_2d_pair(sB, &tmB, b_col, kb * BK, fb);
-            if (!half) tma_load_2d_pair(sB + 64 * BK * 2, &tmB, b_col + 64, kb * BK, fb);
-          } else {
-            tma_load_2d_pair(sB, half ? &tmBh : &tmB, kb * BK, b_col, fb);
+#pragma unroll
+          for (int sub = 0; sub < kPairSub; ++sub) {
+            const int kb = ks * kPairSub + sub;
+            uint8_t *sA = stage_base + stage * kPairStageBytes + sub * kPairSubBytes;
+            uint8_t *sB = sA + kPairABytes;
+            tma_load_2d_pair(sA, &tmA, kb * BK, a_row, fb);
+            if (b_kn) {
+              tma_load_2d_pair(sB, &tmB, b_col, kb * BK, fb);
+              if (!half) tma_load_2d_pair(sB + 64 * BK * 2, &tmB, b_col + 64, kb * BK, fb);
+            } else {
+              tma_load_2d_pair(sB, half ? &tmBh : &tmB, kb * BK, b_col, fb);
+            }
           }
           ++issued;
           if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
@@ -458,15 +470,18 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kAccCols;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int ks = 0; ks < kstages; ++ks) {
           if (!mbar_wait(&bars->full[stage], phase)) { ok = false; break; }
           tc_fence_after();
           const uint32_t soff = (stage * kPairStageBytes) >> 4;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_f16_ss_pair_lohi(d_tmem, da_lo + soff + k * (32 >> 4), da_hi,
-                                 db_lo + soff + k * b_kstep, db_hi, idesc,
-                                 (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < kPairSub * (BK / 16); ++k) {
+            const uint32_t off = soff + (k / (BK / 16)) * (kPairSubBytes >> 4);
+            const int kk = k % (BK / 16);
+            mma_f16_ss_pair_lohi(d_tmem, da_lo + off + kk * (32 >> 4), da_hi,
+                                 db_lo + off + kk * b_kstep, db_hi, idesc,
+                                 (ks | k) != 0 ? 1u : 0u);
+          }
           mma_commit_pair(empty_lead + stage * 8);
           mma_commit_pair(empty_peer + stage * 8);
           if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
