@@ -29,11 +29,18 @@
 // and stores clip, so any shape whose row strides meet TMA's 16-byte rule
 // runs here. Roofline: 2*M*N*K FLOP against the dense fp16/bf16 tensor peak.
 //
-// Measured (clock64 probes on B200): the mainloop is MMA-bound at ~159
-// cycles per N = 256 MMA with A and B from shared memory (a back-to-back
-// probe gives 166-173, the same for cta_group::1 and ::2, any operand
-// layout); the epilogue (~5K cycles per tile) is hidden by the second
-// accumulator. The pair kernel is launched with programmatic stream
+// Measured (clock64 and global-timer traces of the pair kernel on B200): an
+// N = 256 pair MMA takes 128 cycles of the tensor pipe, and the single
+// issuing thread is what limits the mainloop: with descriptors rebuilt per
+// MMA it spent ~150 cycles per MMA, and the tail's half units (half the MMA
+// work) took as long as full units. Descriptors are now built once and
+// advanced by 32-bit adds (~61 cycles per MMA issue), and each barrier stage
+// holds two 64-deep K blocks, so one wait and one commit per CTA serve 8
+// MMAs (a wait ~86 cycles, a commit ~54, measured): 4096^3 1242 -> 1344
+// TFLOP/s per launch. Stage count (4 / 5 / 6 blocks in flight) did not
+// change the unit time; three blocks per stage in two stages was slower.
+// The epilogue (~5K cycles per tile) is hidden by the second accumulator.
+// The pair kernel is launched with programmatic stream
 // serialization, so back-to-back GEMMs overlap the next launch and its set-up
 // with the current one's last wave (400 back-to-back 4096^3 launches: 112.4
 // -> 110.3 us each). With A in TMEM the MMA alone costs 138-140 cycles, but
@@ -282,8 +289,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
 // Same contract, for problems with at least two 128-row blocks: clusters of
 // two CTAs drive one cta_group::2 MMA of M = 256 (128 rows per CTA), N = 256.
 // Each CTA loads its own 128 rows of A and its own 128-column half of the B
-// panel (16 + 16 KiB per 64-deep stage), so a CTA reads 32 KiB from L2 per
-// stage instead of 48 KiB for the same 128 x 256 outputs. CTA 0 issues the
+// panel (16 + 16 KiB per 64-deep K block), so a CTA reads 32 KiB from L2 per
+// block instead of 48 KiB for the same 128 x 256 outputs. CTA 0 issues the
 // MMAs; both CTAs' TMA copies count on CTA 0's full barriers; CTA 0's commits
 // release the empty barriers and accumulator-full barriers of both CTAs; both
 // epilogues release CTA 0's accumulator-empty barriers. Each CTA's TMEM holds
