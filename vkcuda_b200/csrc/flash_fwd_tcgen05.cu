@@ -81,7 +81,10 @@ namespace {
 
 constexpr int BQ = 128;    // query rows per tile (two tiles per CTA)
 constexpr int BKV = 128;   // keys per tile
-constexpr int kStages = 4; // K/V ring depth
+// K/V ring: kStages stages of two tiles each, stage p holding V(p - 1) and
+// K(p) (one load barrier and one release per key step: the issuing thread's
+// barrier waits and commits cost ~86 / ~54 cycles each, measured).
+constexpr int kStages = 2;
 constexpr int kThreads = 320;  // 10 warps: 168 registers per thread at most
                                // (3 warps share one SM sub-partition's 16K)
 constexpr int kWgThreads = 128;
@@ -114,7 +117,7 @@ template <int HD>
 struct FlashSmem {
   static constexpr uint32_t kTile = (HD / 64) * kBoxBytes;  // one Q, K or V tile
   static constexpr uint32_t kQ0 = 0, kQ1 = kTile, kRing = 2 * kTile;
-  static constexpr uint32_t kBars = kRing + kStages * kTile;
+  static constexpr uint32_t kBars = kRing + kStages * 2 * kTile;
   static constexpr size_t kUsed = 1024 + kBars + sizeof(FlashBarriers);
   // At least 120 KiB so that a second CTA never shares the SM: each CTA
   // allocates all 512 TMEM columns.
@@ -204,28 +207,30 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         tma_load_3d(smem + L::kQ1 + c * kBoxBytes, &tmQ, c * 64, qb * 2 * BQ + BQ, bh,
                     &bars->q_full);
       }
-      uint32_t issued = 0;
+      // Stage p = 0..n1: V(p - 1) in its first tile slot (from p = 1), K(p)
+      // in its second (up to p = n1 - 1).
+      int issued = 0;
       bool ok = true;
-      for (int j = 0; ok && j < n1; ++j) {
+      for (int p = 0; p <= n1; ++p) {
+        const int st = p % kStages;
+        if (!mbar_wait(&bars->kv_empty[st], ((p / kStages) & 1) ^ 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bars->kv_full[st], ((p >= 1) + (p < n1)) * L::kTile);
+        uint8_t *slot = smem + L::kRing + st * 2 * L::kTile;
 #pragma unroll
-        for (int kv = 0; kv < 2; ++kv) {
-          const uint32_t idx = 2 * j + kv;
-          const int st = idx % kStages;
-          if (!mbar_wait(&bars->kv_empty[st], ((idx / kStages) & 1u) ^ 1u)) { ok = false; break; }
-          mbar_arrive_expect_tx(&bars->kv_full[st], L::kTile);
-          const CUtensorMap *map = kv ? &tmV : &tmK;
-#pragma unroll
-          for (int c = 0; c < HD / 64; ++c)
-            tma_load_3d(smem + L::kRing + st * L::kTile + c * kBoxBytes, map, c * 64, j * BKV, bh,
+        for (int c = 0; c < HD / 64; ++c) {
+          if (p >= 1)
+            tma_load_3d(slot + c * kBoxBytes, &tmV, c * 64, (p - 1) * BKV, bh, &bars->kv_full[st]);
+          if (p < n1)
+            tma_load_3d(slot + L::kTile + c * kBoxBytes, &tmK, c * 64, p * BKV, bh,
                         &bars->kv_full[st]);
-          ++issued;
         }
+        ++issued;
       }
       mbar_wait(&bars->q_full, 0, 1000000000ull);
-      const uint32_t last = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
-      for (uint32_t i = 0; i < last; ++i) {
-        const uint32_t idx = issued - 1 - i;
-        mbar_wait(&bars->kv_full[idx % kStages], (idx / kStages) & 1u, 1000000000ull);
+      const int last = issued < kStages ? issued : kStages;
+      for (int i = 0; i < last; ++i) {
+        const int p = issued - 1 - i;
+        mbar_wait(&bars->kv_full[p % kStages], (p / kStages) & 1, 1000000000ull);
       }
     }
   } else if (warp == 9) {
@@ -245,9 +250,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       const uint32_t dq0_lo = (uint32_t)dq0, dq1_lo = (uint32_t)dq1;
       const uint32_t dq_hi = (uint32_t)(dq0 >> 32), dk_hi = (uint32_t)(dk0 >> 32);
       const uint32_t dv_hi = (uint32_t)(dv0 >> 32);
-      auto issue_s = [&](int w, uint32_t k_idx) {
+      // K(p) and V(p - 1) of stage p: second and first tile slot.
+      auto issue_s = [&](int w, int p) {
         const uint32_t q_lo = w ? dq1_lo : dq0_lo;
-        const uint32_t k_lo = (uint32_t)dk0 + (((k_idx % kStages) * L::kTile) >> 4);
+        const uint32_t k_lo = (uint32_t)dk0 + ((((p % kStages) * 2 + 1) * L::kTile) >> 4);
         const uint32_t d_tmem = tmem + w * 128;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
@@ -259,8 +265,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
       // O_w += P_w V, part by part (part h: keys h * BKV / kHandoffs ..., in
       // TMEM columns of P_w from h * 64 / kHandoffs), each part as soon as
       // its P has landed.
-      auto issue_pv = [&](int w, uint32_t v_idx, bool accumulate, uint32_t parity, bool last) {
-        const uint32_t v_lo = (uint32_t)dv0 + (((v_idx % kStages) * L::kTile) >> 4);
+      auto issue_pv = [&](int w, int p, bool accumulate, uint32_t parity, bool last) {
+        const uint32_t v_lo = (uint32_t)dv0 + ((((p % kStages) * 2) * L::kTile) >> 4);
         const uint32_t o_tmem = tmem + 256 + w * 128, p_tmem = tmem + w * 128;
         constexpr int kSteps = (BKV / 16) / kHandoffs;  // K = 16 MMAs per part
 #pragma unroll
@@ -278,36 +284,29 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         if (last) mma_commit(&bars->o_full[w]);
         return true;
       };
-      auto wait_full = [&](uint32_t idx) {
-        const bool ok = mbar_wait(&bars->kv_full[idx % kStages], (idx / kStages) & 1u);
+      auto wait_stage = [&](int p) {
+        const bool ok = mbar_wait(&bars->kv_full[p % kStages], (p / kStages) & 1);
         tc_fence_after();
         return ok;
       };
-      bool ok = mbar_wait(&bars->q_full, 0) && wait_full(0);
+      bool ok = mbar_wait(&bars->q_full, 0) && wait_stage(0);
       if (ok) {
         if (n0 > 0) issue_s(0, 0);
         issue_s(1, 0);
         mma_commit(&bars->kv_empty[0]);
       }
+      // Step j: stage j + 1 brings V(j) and K(j + 1); one commit after the
+      // step's last MMA releases it.
       for (int j = 0; ok && j < n1; ++j) {
-        const uint32_t v_idx = 2 * j + 1, k_next = 2 * j + 2;
-        if (!wait_full(v_idx)) break;
-        bool k_ready = false;
+        const int p = j + 1;
+        if (!wait_stage(p)) break;
         if (j < n0) {
-          if (!issue_pv(0, v_idx, j > 0, j & 1, j + 1 == n0)) break;
-          if (j + 1 < n0) {
-            if (!wait_full(k_next)) break;
-            k_ready = true;
-            issue_s(0, k_next);
-          }
+          if (!issue_pv(0, p, j > 0, j & 1, j + 1 == n0)) break;
+          if (j + 1 < n0) issue_s(0, p);
         }
-        if (!issue_pv(1, v_idx, j > 0, j & 1, j + 1 == n1)) break;
-        mma_commit(&bars->kv_empty[v_idx % kStages]);
-        if (j + 1 < n1) {
-          if (!k_ready && !wait_full(k_next)) break;
-          issue_s(1, k_next);
-          mma_commit(&bars->kv_empty[k_next % kStages]);
-        }
+        if (!issue_pv(1, p, j > 0, j & 1, j + 1 == n1)) break;
+        if (j + 1 < n1) issue_s(1, p);
+        mma_commit(&bars->kv_empty[p % kStages]);
       }
     }
   } else {
