@@ -13,8 +13,9 @@
 //   TMEM (512 columns): S0 = Q0 K^T at [0,128), S1 at [128,256), O0 at
 //     [256,384), O1 at [384,512), fp32. The probabilities P_w are written
 //     back as 16-bit pairs over the first 64 columns of S_w.
-//   warp 8      TMA producer: Q0 and Q1 once; K(j), V(j) alternately into a
-//               4-stage ring of 128-row, 128-byte-swizzled tiles.
+//   warp 8      TMA producer: Q0 and Q1 once; then a ring of two stages,
+//               stage p holding V(p-1) and K(p) (128-row, 128-byte-swizzled
+//               tiles), so each key step has one load barrier and one release.
 //   warp 9      allocates TMEM; lane 0 issues the MMAs in the order
 //                 S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) ...
 //               (S_w = Q_w K^T: A and B K-major in shared memory; PV_w:
