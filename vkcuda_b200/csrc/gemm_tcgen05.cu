@@ -451,8 +451,10 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
-      // ---------------- MMA issuer (CTA 0)
+    if (rank == 0) {
+      // ---------------- MMA issuer (CTA 0): the whole warp runs the loop,
+      // one elected lane issues each MMA and commit; waits are made
+      // warp-uniform (a timeout seen by any lane ends the loop for all).
       // Descriptors and the two CTAs' barrier addresses built once and
       // advanced by 32-bit adds: each instruction this thread issues per MMA
       // delays the MMAs (with descriptors rebuilt per MMA the issue pace,
@@ -474,28 +476,28 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         const uint32_t idesc = (u < num_full) ? idesc_full : idesc_half;
-        if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kAccCols;
         for (int ks = 0; ks < kstages; ++ks) {
-          if (!mbar_wait(&bars->full[stage], phase)) { ok = false; break; }
+          if (!__all_sync(0xffffffffu, mbar_wait(&bars->full[stage], phase))) { ok = false; break; }
           tc_fence_after();
           const uint32_t soff = (stage * kPairStageBytes) >> 4;
 #pragma unroll
           for (int k = 0; k < kPairSub * (BK / 16); ++k) {
             const uint32_t off = soff + (k / (BK / 16)) * (kPairSubBytes >> 4);
             const int kk = k % (BK / 16);
-            mma_f16_ss_pair_lohi(d_tmem, da_lo + off + kk * (32 >> 4), da_hi,
+            mma_f16_ss_pair_lohi_warp(d_tmem, da_lo + off + kk * (32 >> 4), da_hi,
                                  db_lo + off + kk * b_kstep, db_hi, idesc,
                                  (ks | k) != 0 ? 1u : 0u);
           }
-          mma_commit_pair(empty_lead + stage * 8);
-          mma_commit_pair(empty_peer + stage * 8);
+          mma_commit_pair_warp(empty_lead + stage * 8);
+          mma_commit_pair_warp(empty_peer + stage * 8);
           if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        mma_commit_pair(lead(&bars->acc_full[acc]));
-        mma_commit_pair(peer(&bars->acc_full[acc]));
+        mma_commit_pair_warp(lead(&bars->acc_full[acc]));
+        mma_commit_pair_warp(peer(&bars->acc_full[acc]));
       }
     }
   } else {
