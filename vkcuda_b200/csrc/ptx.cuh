@@ -288,36 +288,13 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]; kind::f16 (fp16 or bf16 inputs,
-// fp32 accumulate). Issued by a single thread.
-__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc,
-                                           uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Same with the A operand read from TMEM (M rows on lanes, K packed in
-// columns, two 16-bit values per 32-bit column).
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem,
-                                           uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// The same two MMA forms with each shared-memory descriptor passed as its two
-// 32-bit halves: advancing a descriptor within the shared window only changes
-// the address field of the low word, so a loop that steps through operand
-// tiles adds to one 32-bit register per operand and keeps the high words
-// invariant (fewer instructions on the issuing thread per MMA).
+// fp32 accumulate), issued by a single thread. Each shared-memory descriptor
+// is passed as its two 32-bit halves: advancing a descriptor within the
+// shared window only changes the address field of the low word, so a loop
+// that steps through operand tiles adds to one 32-bit register per operand
+// and keeps the high words invariant (fewer instructions on the issuing
+// thread per MMA). The _ts form reads the A operand from TMEM (M rows on
+// lanes, K packed in columns, two 16-bit values per 32-bit column).
 __device__ __forceinline__ void mma_f16_ss_lohi(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
                                                 uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
                                                 uint32_t accumulate) {
@@ -528,20 +505,9 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
                : "memory");
 }
 
-// Pair MMA (M = 256 across the two CTAs), issued by one thread of CTA 0.
-__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc,
-                                                uint64_t b_desc, uint32_t idesc,
-                                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Pair MMA with each shared-memory descriptor passed as two 32-bit halves
-// (as mma_f16_ss_lohi).
+// Pair MMA (M = 256 across the two CTAs, each CTA's shared memory holding
+// its A rows and half of B), issued by one thread of CTA 0; descriptors as
+// two 32-bit halves (as mma_f16_ss_lohi).
 __device__ __forceinline__ void mma_f16_ss_pair_lohi(uint32_t d_tmem, uint32_t a_lo,
                                                      uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
                                                      uint32_t idesc, uint32_t accumulate) {
@@ -579,19 +545,8 @@ __device__ __forceinline__ void mma_commit_pair_warp(uint32_t bar_cluster_addr) 
       : "memory");
 }
 
-// Pair MMA of kind::tf32 (K = 8 per instruction), issued by one thread of CTA 0.
-__device__ __forceinline__ void mma_tf32_ss_pair(uint32_t d_tmem, uint64_t a_desc,
-                                                 uint64_t b_desc, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// As mma_tf32_ss_pair with each descriptor passed as two 32-bit halves.
+// Pair MMA of kind::tf32 (K = 8 per instruction, M = 256 across the two
+// CTAs), issued by one thread of CTA 0; descriptors as two 32-bit halves.
 __device__ __forceinline__ void mma_tf32_ss_pair_lohi(uint32_t d_tmem, uint32_t a_lo,
                                                       uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
                                                       uint32_t idesc, uint32_t accumulate) {
@@ -611,18 +566,6 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster_addr) {
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           bar_cluster_addr)
       : "memory");
-}
-
-// Per-warpgroup register reallocation (all four warps of the warpgroup
-// execute it). The launch-time total (threads x registers at launch) bounds
-// the sum of the warpgroups' shares.
-template <uint32_t R>
-__device__ __forceinline__ void regs_increase() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
-}
-template <uint32_t R>
-__device__ __forceinline__ void regs_decrease() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R));
 }
 
 // Packed two-lane fp32 arithmetic (sm_100 f32x2): one instruction for two
