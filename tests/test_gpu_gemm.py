@@ -103,7 +103,11 @@ def _run_gemm(gpu, dev, orc, M, N, K, bf16, b_kn, with_c=False, lda=None, ldb=No
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 512), (300, 500, 200),
-                                   (1, 1, 1), (129, 257, 1000), (1024, 1024, 1024), (37, 8, 72)])
+                                   (1, 1, 1), (129, 257, 1000), (1024, 1024, 1024), (37, 8, 72),
+                                   # CTA-pair kernel with an odd number of 64-deep K
+                                   # blocks: the last barrier stage's second block
+                                   # lies past K (zero-filled)
+                                   (256, 256, 192), (384, 768, 320)])
 @pytest.mark.parametrize("bf16", [False, True])
 @pytest.mark.parametrize("b_kn", [True, False])
 def test_gemm_random_vs_oracle(gpu, dev, orc, M, N, K, bf16, b_kn):
