@@ -453,7 +453,7 @@ def gemm_e2e(vc, dist, steps, warmup):
             "d2h_bytes_per_step": nb32, "ms_per_step": round(ms / steps, 4),
             "path": "vcMallocHost + vcMemcpyAsyncS + vcLaunchKernel(vc.gemm) + vcMemcpyAsyncS; "
                     f"upload, GEMM and download streams ordered by vcEvents over {E2E_LANES} "
-                    "buffer sets; bound: PCIe Gen5 x16 at ~48 GB/s each way with both "
+                    "buffer sets; bound: PCIe Gen5 x16, 44-48 GB/s each way with both "
                     "directions busy (64 MiB each way per step)"}
 
 
