@@ -15,7 +15,9 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 SUM_RTOL = 1e-6
 
 
-@pytest.mark.parametrize("n", [0, 1, 3, 64, 1000, 1 << 20, (1 << 22) + 7])
+# (1 << 25) + 12345: the bulk-copy kernel, with a tail past its last whole
+# 2048-element chunk
+@pytest.mark.parametrize("n", [0, 1, 3, 64, 1000, 1 << 20, (1 << 22) + 7, (1 << 25) + 12345])
 def test_vadd_bit_exact(gpu, dev, orc, n):
     rng = np.random.default_rng(n)
     a = rng.random(n, dtype=np.float32)
@@ -53,7 +55,7 @@ def test_sum_within_1e6(gpu, dev, orc, n):
     assert got == pytest.approx(ref, rel=SUM_RTOL, abs=1e-12)
 
 
-@pytest.mark.parametrize("n", [7, 1 << 20, 3_000_001])
+@pytest.mark.parametrize("n", [7, 1 << 20, 3_000_001, 1 << 25, (1 << 25) + 12345])
 def test_vadd_sum_fused(gpu, dev, orc, n):
     rng = np.random.default_rng(n)
     a = rng.random(n, dtype=np.float32)
