@@ -90,7 +90,7 @@ def _torch_ref_fp32(q, k, v, causal):
         return F.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal)
 
 
-def test_flash_config3_all_rows_vs_torch(gpu):
+def test_flash_causal_fp16_8x16x4096_all_rows_vs_torch(gpu):
     """B=8, H=16, N=4096, d=128, fp16, causal: every row against torch fp32."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(33)
@@ -108,7 +108,7 @@ def test_flash_config3_all_rows_vs_torch(gpu):
     assert worst <= 2e-3, worst
 
 
-def test_flash_config4_slices_vs_torch(gpu):
+def test_flash_bf16_32x32x8192_slices_vs_torch(gpu):
     """B=32, H=32, N=8192, d=128, bf16 (inputs 0.5 N(0,1)): 128 of the 1024
     slices (the first and last 64) against torch fp32."""
     import torch

@@ -165,15 +165,15 @@ def test_flash_tcgen05_large_scores_rescale(gpu, dev, orc):
     _run_tc(gpu, dev, orc, 2, 512, 128, True, True, seed=4, qk_scale=4.0)
 
 
-def test_flash_tcgen05_config3_sampled(gpu, dev, orc):
-    """Benchmark config: fp16, B=8, H=16, N=4096, d=128, causal; rows checked
+def test_flash_tcgen05_causal_fp16_8x16x4096_sampled(gpu, dev, orc):
+    """The causal fp16 benchmark workload: B=8, H=16, N=4096, d=128; rows checked
     on a sample (4 slices x 64 rows, including the last rows of the sequence)."""
     _run_tc(gpu, dev, orc, 128, 4096, 128, True, False, seed=3, bh_check=(60, 64),
             row_check=(4032, 4096))
 
 
-def test_flash_tcgen05_config4_full_shape_sampled(gpu, orc):
-    """Benchmark config 4 at its own shape: bf16, B=32, H=32 (1024 slices),
+def test_flash_tcgen05_bf16_32x32x8192_full_shape_sampled(gpu, orc):
+    """The bf16 attention benchmark workload at its own shape: B=32, H=32 (1024 slices),
     N=8192, d=128, non-causal, Q/K/V ~ 0.5 N(0,1) rounded to bf16 (2 GiB per
     tensor, generated on the device). The whole launch runs; the fp64 oracle
     checks 4 slices (the first, the last, and both sides of an 8-GPU shard
